@@ -1,0 +1,519 @@
+#!/usr/bin/env python
+"""Benchmark of the Domino per-block draft step on B200.
+
+One step = the draft side of one speculative block (block 16) for every row
+of the batch, through the public API (``DraftCorrectionGraphRunner.draft_block``
++ ``.accept``, i.e. ``dd_draft_block`` + ``dd_accept``):
+
+  lm_head base logits for the 15 draft positions  ->  z = hiddens @ W_z^T
+  ->  h0 = GRU(last token)  ->  15 x [ s = h W_s^T -> SiLU mid -> fc2 + base
+  -> argmax -> GRU step ]  ->  greedy acceptance against the target's tokens.
+
+Workload (default): the Qwen3-8B-shaped draft head, bf16, batch 1 per GPU,
+H = G = 4096, E = 12288, V = 151936, seeded random-init weights N(0, 0.02),
+hidden states N(0, 1), target tokens equal to the draft's own tokens for the
+first k ~ U{0..15} positions and different after.  The weights streamed every
+step (8.7 GB) are ~70x the 126 MB L2, so no L2 flush is needed between steps.
+
+Multi-GPU: one process per GPU, each runs its own batch (requests are
+independent; no collective on the data path): weak scaling.  Times are CUDA
+events on each rank, max over ranks.
+
+``--impl reference`` times the CPU oracle (a numpy restatement of the
+reference's draft step) on this host's cores on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "draft tokens/sec per GPU & µs per draft block (block=16) at 1/2/4/8 B200; HBM/TC roofline %"
+MODELS = {
+    "qwen3-8b": dict(H=4096, G=4096, E=12288, V=151936),
+    "qwen3-4b": dict(H=2560, G=2560, E=6912, V=151936),
+    "qwen3.6-27b": dict(H=5120, G=5120, E=17408, V=151936),
+}
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model", choices=sorted(MODELS), default="qwen3-8b")
+    ap.add_argument("--batch", type=int, default=1, help="rows per GPU")
+    ap.add_argument("--emb-dim", type=int, default=None, help="override E (correction-MLP width)")
+    ap.add_argument("--block", type=int, default=16)
+    ap.add_argument("--prefix-len", type=int, default=0, help="pure_draft_prefix_len")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=150.0)
+    return ap.parse_args()
+
+
+def shapes(args):
+    m = dict(MODELS[args.model])
+    if args.emb_dim:
+        m["E"] = args.emb_dim
+    S = args.block - 1 - args.prefix_len
+    return m["H"], m["G"], m["E"], m["V"], S, args.prefix_len
+
+
+def algorithmic_bytes(B, H, G, E, V, S, P, w=2):
+    """Bytes the draft step must move per block (weights once per use)."""
+    K = S + P
+    weights = V * H + E * H + S * (E * G + V * E) + max(0, S + P - 1) * 3 * G * G
+    acts = 2 * B * K * V * 2          # base logits written + read
+    acts += B * (S + P) * 3 * G * 2   # gathered table rows
+    acts += B * K * H * 2 + B * K * E * 2 * 2  # hidden states read, z written + read
+    return weights * w + acts
+
+
+def fc2_bytes(B, E, V, w=2):
+    """Algorithmic bytes of one fc2 phase launch: fc2 once + one base-logit row per batch row."""
+    return V * E * w + B * V * 2
+
+
+def workload_name(args, B, H, G, E, V, S, P):
+    return (f"{args.model}-shaped Domino draft head, bf16, batch {B}/GPU, block {args.block} "
+            f"({S} draft + {P} prefix tokens), H={H} G={G} E={E} V={V}")
+
+
+def measured_peak_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(model, B, E):
+    """Per-launch DRAM bytes of the fc2 phase from a committed ncu summary, or None."""
+    path = os.path.join(ROOT, "profiles", "fc2_phase_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        rec = d.get(f"{model}:B{B}:E{E}")
+        return None if rec is None else float(rec["dram_bytes_per_launch"])
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"dd_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- distributed
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------- model construction
+def build_modules(H, G, E, V, device, seed):
+    import torch
+    import torch.nn as nn
+
+    class DraftHead(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.prefix_gru = nn.GRU(H, G, num_layers=1, batch_first=True, bias=False, device=device,
+                                     dtype=torch.bfloat16)
+            self.embed_proj = nn.Sequential(
+                nn.Linear(H + G, E, bias=False, device=device, dtype=torch.bfloat16), nn.SiLU(),
+                nn.Linear(E, V, bias=False, device=device, dtype=torch.bfloat16))
+
+    class Target(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.model = nn.Module()
+            self.model.embed_tokens = nn.Embedding(V, H, device=device, dtype=torch.bfloat16)
+            self.lm_head = nn.Linear(H, V, bias=False, device=device, dtype=torch.bfloat16)
+
+    g = torch.Generator(device=device).manual_seed(seed)
+    draft, target = DraftHead(), Target()
+    with torch.no_grad():
+        for p in list(draft.parameters()) + [target.lm_head.weight]:
+            p.normal_(0.0, 0.02, generator=g)
+        target.model.embed_tokens.weight.normal_(0.0, 1.0, generator=g)
+    return draft.eval(), target.eval()
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    from domino_b200 import DraftCorrectionGraphRunner, _lib
+
+    H, G, E, V, S, P = shapes(args)
+    B = args.batch
+    K = S + P
+    draft, target = build_modules(H, G, E, V, device, args.seed + 17 * rank)
+    runner = DraftCorrectionGraphRunner(draft, target, B, S, H, G, V, P + 1, device, use_graph=False)
+    lib = _lib.load()
+
+    # Synthetic inputs: a pool of blocks; the target agrees with the draft on
+    # the first k ~ U{0..S} positions (the path is deterministic, so a first
+    # pass gives the draft tokens the posterior is built from).
+    n_pool = 8
+    g = torch.Generator(device=device).manual_seed(args.seed + 1000 + rank)
+    ph_pool = [torch.randn(B, K, H, generator=g, device=device).to(torch.bfloat16) for _ in range(n_pool)]
+    last_pool = [torch.randint(0, V, (B,), generator=g, device=device) for _ in range(n_pool)]
+    post_pool, kk = [], []
+    for i in range(n_pool):
+        verify, _ = runner.draft_block(last_pool[i], ph_pool[i])
+        k = torch.randint(0, S + 1, (B,), generator=g, device=device)
+        post = torch.randint(0, V, (B, K + 1), generator=g, device=device)
+        pos = torch.arange(K + 1, device=device).unsqueeze(0)
+        agree = pos < (P + k).unsqueeze(1)
+        shifted = torch.cat([verify[:, 1:], verify[:, -1:]], 1)
+        post = torch.where(agree, shifted, torch.where(post == shifted, (post + 1) % V, post))
+        post_pool.append(post)
+        kk.append(k)
+    torch.cuda.synchronize()
+    base_buf = torch.empty(B, K, V, dtype=torch.bfloat16, device=device)
+
+    def step(i):
+        verify, _ = runner.draft_block(last_pool[i], ph_pool[i], base_buf)
+        return runner.accept(verify, post_pool[i])
+
+    # ---- value: device-resident inputs
+    for i in range(args.warmup):
+        step(i % n_pool)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    if rank == 0:
+        clocks.start()
+        time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    hist = [0] * (S + 2)
+    accs = []
+    for i in range(args.steps):
+        acc, _ = step(i % n_pool)
+        accs.append(acc)
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    for a in accs[: n_pool]:
+        for x in a.tolist():
+            hist[min(x + 1, S + 1)] += 1
+
+    # ---- e2e: pinned host inputs, H2D + D2H inside the timed region
+    ph_host = [t.cpu().pin_memory() for t in ph_pool]
+    last_host = [t.cpu().pin_memory() for t in last_pool]
+    post_host = [t.cpu().pin_memory() for t in post_pool]
+    ph_dev = torch.empty_like(ph_pool[0])
+    last_dev = torch.empty_like(last_pool[0])
+    post_dev = torch.empty_like(post_pool[0])
+    verify_host = torch.empty(B, K + 1, dtype=torch.long).pin_memory()
+    acc_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    bonus_host = torch.empty(B, dtype=torch.long).pin_memory()
+
+    def e2e_step(i):
+        ph_dev.copy_(ph_host[i], non_blocking=True)
+        last_dev.copy_(last_host[i], non_blocking=True)
+        post_dev.copy_(post_host[i], non_blocking=True)
+        verify, _ = runner.draft_block(last_dev, ph_dev, base_buf)
+        acc, bonus = runner.accept(verify, post_dev)
+        verify_host.copy_(verify, non_blocking=True)
+        acc_host.copy_(acc, non_blocking=True)
+        bonus_host.copy_(bonus, non_blocking=True)
+
+    for i in range(min(args.warmup, 3)):
+        e2e_step(i % n_pool)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev2.record()
+    for i in range(args.steps):
+        e2e_step(i % n_pool)
+    ev3.record()
+    torch.cuda.synchronize()
+    ms_e2e = ev2.elapsed_time(ev3)
+    clk = clocks.stop() if rank == 0 else None
+    h2d = ph_pool[0].numel() * 2 + B * 8 + B * (K + 1) * 8
+    d2h = B * (K + 1) * 8 + B * 4 + B * 8
+
+    # ---- per-launch timing (events around every launch; separate loop)
+    lib.dd_set_timing(runner._h, 1)
+    n_timed_blocks = 3
+    for i in range(n_timed_blocks):
+        step(i % n_pool)
+    torch.cuda.synchronize()
+    kinds = (ctypes.c_int32 * 4096)()
+    durs = (ctypes.c_float * 4096)()
+    n = _lib.check(lib.dd_read_timing(runner._h, kinds, durs, 4096), runner._h, "dd_read_timing")
+    lib.dd_set_timing(runner._h, 0)
+    per_kind = {}
+    for i in range(n):
+        per_kind.setdefault(_lib.PHASES.get(kinds[i], str(kinds[i])), []).append(durs[i])
+    launches_per_step = n / n_timed_blocks + 1  # + the accept kernel
+    status = runner.status()
+
+    # ---- reduce over ranks: max time
+    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        st = torch.tensor([status], device=device)
+        dist.all_reduce(st, op=dist.ReduceOp.MAX)
+        status = int(st.item())
+    ms, ms_e2e = float(t[0]), float(t[1])
+
+    if rank == 0:
+        tokens = world * B * S * args.steps
+        value = tokens / (ms / 1e3)
+        e2e_value = tokens / (ms_e2e / 1e3)
+        peak, peak_src = measured_peak_hbm()
+        fc2_ms = statistics.mean(per_kind.get("fc2", [float("nan")]))
+        fc2_b = fc2_bytes(B, E, V)
+        achieved = fc2_b / (fc2_ms / 1e3) / 1e9
+        step_b = algorithmic_bytes(B, H, G, E, V, S, P)
+        step_ms = ms / args.steps
+        traffic = committed_traffic(args.model, B, E)
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "draft tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(step_ms, 4),
+            "us_per_block": round(step_ms * 1e3, 1),
+            "per_gpu_value": round(value / world, 2),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1), "
+                    "target tokens = draft tokens for the first k~U{0..15} positions",
+            "config": {
+                "workload": workload_name(args, B, H, G, E, V, S, P),
+                "batch_per_gpu": B, "global_batch": world * B, "block": args.block, "seq_len": args.block,
+                "parallelism": f"dp{world} (request batch sharded, no collective)",
+                "l2": "no flush: 8.7 GB of weights streamed per step, ~70x the 126 MB L2",
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "fc2 phase (gemv_stream_kernel PH_FC2)",
+                "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_src, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": fc2_b, "avg_launch_ms": round(fc2_ms, 4),
+            },
+            "step_roofline": {
+                "algorithmic_bytes_per_step": step_b,
+                "achieved_gbs": round(step_b / (step_ms / 1e3) / 1e9, 1),
+                "frac": round(step_b / (step_ms / 1e3) / 1e9 / peak, 4),
+            },
+            "phase_ms": {k: round(statistics.mean(v), 4) for k, v in sorted(per_kind.items())},
+            "phase_launches_per_block": {k: len(v) / n_timed_blocks for k, v in sorted(per_kind.items())},
+            "e2e": {"value": round(e2e_value, 2), "unit": "draft tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e / args.steps, 4)},
+            "gpu_launches": int(round(launches_per_step * args.steps)),
+            "accept_hist": hist,
+            "device_status": status,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args, draft, target, ph_pool[0], last_pool[0], budget_s=30.0)
+        print(json.dumps(line), flush=True)
+    runner.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- CPU oracle
+def oracle_setup(draft, target, P):
+    """fp32 host copies of the head weights for the numpy oracle."""
+    from oracle import draft_oracle as O
+
+    def f32(t):
+        return t.detach().float().cpu().numpy()
+
+    fc1 = draft.embed_proj[0].weight
+    w = O.DraftWeights(fc1=f32(fc1), fc2=f32(draft.embed_proj[2].weight), w_ih=f32(draft.prefix_gru.weight_ih_l0),
+                       w_hh=f32(draft.prefix_gru.weight_hh_l0), embed=None, dtype="bf16")
+    import torch
+    tab = torch.nn.functional.linear(target.model.embed_tokens.weight, draft.prefix_gru.weight_ih_l0)
+    w.table = f32(tab)
+    del tab
+    return w, f32(target.lm_head.weight)
+
+
+def oracle_block(w, lm, ph, last, S, P):
+    """One block of the oracle: lm_head, pure-draft prefix, rollout."""
+    from oracle import draft_oracle as O
+    import numpy as np
+
+    base = O.lm_head(ph, lm, "bf16")
+    pre = O.pure_draft_prefix(base, P) if P else np.zeros((ph.shape[0], 0), np.int64)
+    prefix = np.concatenate([last.reshape(-1, 1), pre], 1)
+    tr = O.rollout(w, prefix, ph[:, P:], base[:, P:])
+    return tr.tokens
+
+
+def cpu_baseline(args, draft, target, ph, last, budget_s):
+    """Time the oracle on this host's cores on blocks of the same workload."""
+    import numpy as np
+
+    H, G, E, V, S, P = shapes(args)
+    w, lm = oracle_setup(draft, target, P)
+    w.embed = np.zeros((1, H), np.float32)  # H is read from embed's shape; the table is given
+    ph_np = ph.float().cpu().numpy()
+    last_np = last.cpu().numpy()
+    blocks, t0 = 0, time.perf_counter()
+    while True:
+        oracle_block(w, lm, ph_np, last_np, S, P)
+        blocks += 1
+        if time.perf_counter() - t0 > budget_s / 3 or blocks >= 3:
+            break
+    dt = time.perf_counter() - t0
+    return {
+        "value": round(blocks * args.batch * S / dt, 4), "unit": "draft tokens/s", "cores": os.cpu_count(),
+        "kind": "port", "threads": "numpy BLAS, all host threads",
+        "sample": f"{blocks} full block(s) of the same workload (batch {args.batch}, {S} draft tokens each) "
+                  f"through oracle/draft_oracle.py in fp32 numpy, {dt:.1f} s",
+    }
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+    import torch
+
+    H, G, E, V, S, P = shapes(args)
+    B = args.batch
+    K = S + P
+    dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
+    # Weights are generated on the GPU only for speed; everything timed runs on the host.
+    draft, target = build_modules(H, G, E, V, dev, args.seed)
+    w, lm = oracle_setup(draft, target, P)
+    w.embed = np.zeros((1, H), np.float32)
+    del draft, target
+    rng = np.random.default_rng(args.seed)
+    from oracle.draft_oracle import round_to
+    blocks = [(round_to(rng.standard_normal((B, K, H)).astype(np.float32), "bf16"),
+               rng.integers(0, V, (B,))) for _ in range(2)]
+    t0 = time.perf_counter()
+    oracle_block(w, lm, blocks[0][0], blocks[0][1], S, P)
+    t_block = time.perf_counter() - t0
+    n_steps = max(1, min(args.steps, int(args.cpu_budget_s / max(t_block, 1e-3))))
+    n_warm = min(args.warmup, 1)
+    for i in range(n_warm):
+        oracle_block(w, lm, *blocks[i % 2], S, P)
+    t0 = time.perf_counter()
+    for i in range(n_steps):
+        oracle_block(w, lm, *blocks[i % 2], S, P)
+    dt = time.perf_counter() - t0
+    value = n_steps * B * S / dt
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "draft tokens/s",
+        "n_gpus": world,
+        "steps": n_steps,
+        "warmup": n_warm,
+        "ms_per_step": round(dt / n_steps * 1e3, 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16 values in fp32 numpy",
+        "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1)",
+        "config": {"workload": workload_name(args, B, H, G, E, V, S, P), "batch_per_gpu": B,
+                   "global_batch": B, "block": args.block, "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "draft tokens/s", "cores": os.cpu_count(),
+                         "kind": "port",
+                         "sample": f"{n_steps} block(s) of batch {B} (of {args.steps} requested; capped at "
+                                   f"~{args.cpu_budget_s:.0f} s), oracle/draft_oracle.py fp32 numpy, all host threads"},
+        "e2e": {"value": round(value, 4), "unit": "draft tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

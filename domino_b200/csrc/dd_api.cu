@@ -1,0 +1,668 @@
+// dd_api.cu -- host side of libdomino_draft.so: the handle, TMA descriptors,
+// the launch sequence of one draft step, and the C ABI of
+// include/domino_draft.h.
+//
+// Launch sequence of one rollout (code/kernel/domino.py:374-431), all on the
+// caller's stream, each launch with programmatic dependent launch so that a
+// phase's weight stream starts before the previous phase has finished:
+//
+//   memset(argmax words)
+//   Z     gemv  z = parallel_hiddens @ W_z^T (+ fc1 bias)          [B*S, E]
+//   P0    cell  h0 = GRU(table[prefix_ids[:, 0]], h = 0)
+//   (Pj   gemv  gh = h W_hh^T ; cell h = GRU(table[prefix_ids[:, j]], h))  j = 1..p
+//   for t in 0..S-1:
+//     SGH gemv  s = h W_s^T -> mid = SiLU(z_t + s) as (hi, lo) rows ;  gh = h W_hh^T
+//     FC2 gemv  logit = fc2 (hi + lo) + fc2_bias + base_t -> atomicMax argmax word
+//     CELL      token_t -> out ; h = GRU(table[token_t], gh, h)
+//
+// dd_draft_block replaces the Z launch by one that also computes the base
+// logits (lm_head) and the pure-draft prefix argmax.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/domino_draft.h"
+#include "dd_cell.cuh"
+#include "dd_gemv.cuh"
+
+using namespace dd;
+
+namespace {
+
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                     const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                     CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+PFN_encodeTiled g_encode = nullptr;
+std::once_flag g_encode_once;
+char g_global_error[256] = "";
+
+int round_up(int x, int m) { return (x + m - 1) / m * m; }
+int ceil_div(long long x, long long m) { return (int)((x + m - 1) / m); }
+
+}  // namespace
+
+struct dd_handle {
+  int device = 0;
+  int num_sms = 0;
+  dd_config cfg{};
+  dd_weights w{};
+  bool have_weights = false;
+  int N1 = 16;  // MMA N of the h operand: batch rows padded to 16
+  int N2 = 16;  // MMA N of the mid operand: 2 * batch (hi, lo) padded to 16
+  int nslots = 0;
+  void* zbuf = nullptr;       // [B * (p + S), E]
+  void* midbuf = nullptr;     // [N2, E] rows 2b = hi, 2b+1 = lo, rest zero
+  void* hbuf[2] = {nullptr, nullptr};  // [N1, G], rows >= B zero
+  void* ghbuf = nullptr;      // [B, 3G]
+  unsigned long long* slots = nullptr;  // [B, nslots]
+  float* partials = nullptr;  // [2 * num_sms, 256, 128]
+  unsigned int* counters = nullptr;
+  int max_tiles = 0;
+  unsigned int* status = nullptr;
+  CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
+  // Opt-in per-launch timing (dd_set_timing): an event pair around each launch.
+  static constexpr int kMaxTimed = 4096;
+  bool timing = false;
+  int n_timed = 0;
+  int timed_kind[kMaxTimed];
+  cudaEvent_t ev[2 * kMaxTimed] = {};
+  char err[256] = "";
+};
+
+namespace {
+
+int fail(dd_handle* h, int code, const char* fmt, ...) {
+  char* dst = h ? h->err : g_global_error;
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(dst, 256, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+#define DD_CUDA(h, call)                                                                   \
+  do {                                                                                     \
+    cudaError_t e_ = (call);                                                               \
+    if (e_ != cudaSuccess) return fail((h), DD_ECUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+  } while (0)
+
+int ensure_encoder(dd_handle* h) {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_encodeTiled>(fn);
+  });
+  if (!g_encode) return fail(h, DD_ECUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  return DD_OK;
+}
+
+// 2-D K-major tile map: rows of `k` elements (row stride `ld` elements),
+// boxes of 64 x box_rows with 128-byte swizzle; out-of-range reads are zero.
+int encode_kmajor(dd_handle* h, CUtensorMap* m, const void* ptr, int dtype, long long k, long long rows,
+                  long long ld, int box_rows) {
+  if (!ptr) return fail(h, DD_EINVAL, "null tensor pointer");
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return fail(h, DD_EINVAL, "tensor base is not 16-byte aligned");
+  if ((ld * 2) % 16 != 0) return fail(h, DD_EINVAL, "row stride %lld elements is not a multiple of 16 bytes", ld);
+  if (k <= 0 || rows <= 0 || ld < k) return fail(h, DD_EINVAL, "bad tensor shape k=%lld rows=%lld ld=%lld", k, rows, ld);
+  if (box_rows < 1 || box_rows > 256) return fail(h, DD_EINVAL, "bad box rows %d", box_rows);
+  int rc = ensure_encoder(h);
+  if (rc) return rc;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)kChunkK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, dtype == DD_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                        const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, DD_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DD_OK;
+}
+
+enum class PhaseClass { Big, Small };
+
+int timing_begin(dd_handle* h, int kind, cudaStream_t st) {
+  if (!h->timing) return DD_OK;
+  if (h->n_timed >= dd_handle::kMaxTimed) return fail(h, DD_EINVAL, "timing record is full; call dd_read_timing");
+  const int i = h->n_timed;
+  for (int k = 0; k < 2; ++k)
+    if (!h->ev[2 * i + k]) DD_CUDA(h, cudaEventCreate(&h->ev[2 * i + k]));
+  h->timed_kind[i] = kind;
+  DD_CUDA(h, cudaEventRecord(h->ev[2 * i], st));
+  return DD_OK;
+}
+
+int timing_end(dd_handle* h, cudaStream_t st) {
+  if (!h->timing) return DD_OK;
+  DD_CUDA(h, cudaEventRecord(h->ev[2 * h->n_timed + 1], st));
+  ++h->n_timed;
+  return DD_OK;
+}
+
+// Opt the gemv kernel into the full 227 KB of dynamic shared memory, once
+// per (device, element type).
+template <typename T, int kPhase>
+int set_kernel_attrs(dd_handle* h) {
+  static bool done[64] = {};
+  const int d = h->device & 63;
+  if (!done[d]) {
+    DD_CUDA(h, cudaFuncSetAttribute(gemv_stream_kernel<T, kPhase>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    227 * 1024));
+    done[d] = true;
+  }
+  return DD_OK;
+}
+
+// Every launch carries programmatic stream serialisation, so it may start
+// while the previous kernel on the stream drains (see griddepcontrol.* in
+// the kernels).
+struct Launch {
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  Launch(dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+};
+
+// Fill the pass-independent launch fields of a gemv phase and launch it.
+template <typename T, int kPhase>
+int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, const CUtensorMap& b, GemvParams p,
+                PhaseClass cls, bool allow_split, cudaStream_t st) {
+  p.KC = ceil_div(p.K, kChunkK);
+  int tiles = 0;
+  for (int s = 0; s < p.nseg; ++s) {
+    p.seg[s].tiles = ceil_div(p.seg[s].rows, kTileM);
+    tiles += p.seg[s].tiles;
+  }
+  if (tiles > h->max_tiles) return fail(h, DD_EINVAL, "phase has %d tiles > %d", tiles, h->max_tiles);
+  p.units = (long long)tiles * p.KC;
+  int grid = (int)std::min<long long>(h->num_sms, allow_split ? p.units : tiles);
+  if (grid < 1) grid = 1;
+  p.b_bytes = (uint32_t)p.N * 128u;
+  p.stage_bytes = kATileBytes + p.b_bytes;
+  const uint32_t ring_budget = p.N > 64 ? 196u * 1024u : (cls == PhaseClass::Big ? 110u * 1024u : 100u * 1024u);
+  p.stages = std::max(2, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  p.acc_slots = p.N <= 128 ? 2 : 1;
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(p.acc_slots * p.N)) cols <<= 1;
+  p.tmem_cols = cols;
+  p.idesc = idesc_f16((uint32_t)p.N, std::is_same<T, __half>::value ? 0u : 1u);
+  p.partials = h->partials;
+  p.tile_counters = h->counters;
+  p.status = h->status;
+  size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + kSmemTail;
+  // Big phases reserve enough shared memory that two CTAs of the same phase
+  // never share an SM, while one small-phase CTA still fits beside them.
+  if (cls == PhaseClass::Big && smem < 118 * 1024) smem = 118 * 1024;
+  int rc = set_kernel_attrs<T, kPhase>(h);
+  if (rc) return rc;
+  rc = timing_begin(h, kPhase, st);
+  if (rc) return rc;
+  Launch L(dim3(grid), dim3(kThreads), smem, st);
+  DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, gemv_stream_kernel<T, kPhase>, a0, a1 ? *a1 : a0, b, p));
+  return timing_end(h, st);
+}
+
+template <typename T>
+int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
+  cp.B = h->cfg.batch;
+  cp.G = h->cfg.gru_hidden;
+  cp.V = h->cfg.vocab;
+  cp.table = h->w.table;
+  cp.table_ld = h->w.table_ld;
+  cp.b_hh = h->w.b_hh;
+  cp.status = h->status;
+  const int threads = cp.B * (cp.G / 8);
+  int rc = timing_begin(h, DD_PHASE_CELL, st);
+  if (rc) return rc;
+  Launch L(dim3(ceil_div(threads, 128)), dim3(128), 0, st);
+  DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, cell_kernel<T>, cp));
+  return timing_end(h, st);
+}
+
+GemvParams base_params(const dd_handle* h) {
+  GemvParams p;
+  memset(&p, 0, sizeof(p));
+  p.B = h->cfg.batch;
+  p.V = h->cfg.vocab;
+  p.E = h->cfg.emb_dim;
+  p.G3 = 3 * h->cfg.gru_hidden;
+  p.slots = h->slots;
+  p.nslots = h->nslots;
+  return p;
+}
+
+// Z (+ lm_head) phase over the X = parallel_hiddens rows, in passes of <= 256 rows.
+template <typename T>
+int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* base_out, cudaStream_t st) {
+  const dd_config& c = h->cfg;
+  const int rows = c.batch * positions;
+  CUtensorMap tm_x;
+  const int n_pass = std::min(256, round_up(rows, 16));
+  int rc = encode_kmajor(h, &tm_x, ph, c.dtype, c.hidden, rows, c.hidden, n_pass);
+  if (rc) return rc;
+  for (int n_off = 0; n_off < rows; n_off += 256) {
+    GemvParams p = base_params(h);
+    const int n_valid = std::min(256, rows - n_off);
+    p.N = n_pass;  // == the TMA box height, so expect_tx matches the bytes every load delivers
+    p.n_off = n_off;
+    p.n_valid = n_valid;
+    p.K = c.hidden;
+    p.z_out = h->zbuf;
+    p.fc1_bias = h->w.fc1_bias;
+    if (base_out) {
+      p.nseg = 2;
+      p.seg[0] = {c.vocab, 0, EPI_LMHEAD};
+      p.seg[1] = {c.emb_dim, 0, EPI_ZPROJ};
+      p.base_out = base_out;
+      p.kpos = positions;
+      p.npre = npre;
+      rc = launch_gemv<T, PH_ZLM>(h, h->tm_lm, &h->tm_wz, tm_x, p, PhaseClass::Big, true, st);
+    } else {
+      p.nseg = 1;
+      p.seg[0] = {c.emb_dim, 0, EPI_ZPROJ};
+      rc = launch_gemv<T, PH_Z>(h, h->tm_wz, nullptr, tm_x, p, PhaseClass::Big, true, st);
+    }
+    if (rc) return rc;
+  }
+  return DD_OK;
+}
+
+// GRU prefix + S rollout steps.  Token sources: ids (runner) or the prefix
+// argmax words (draft block); outputs to out[b * out_ld + out_col0 + t].
+template <typename T>
+int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, int npre, int positions,
+                const void* base, int64_t* out, int out_ld, int out_col0, int64_t* prefix_out, cudaStream_t st) {
+  const dd_config& c = h->cfg;
+  int rc;
+  int cur = 0;
+  // h0 from the first prefix token, zero state.
+  {
+    CellParams cp;
+    memset(&cp, 0, sizeof(cp));
+    cp.src = 0;
+    cp.ids = ids;
+    cp.ids_ld = ids_ld;
+    cp.ids_col = 0;
+    cp.out = prefix_out;
+    cp.out_ld = out_ld;
+    cp.out_col = 0;
+    cp.h_zero = 1;
+    cp.write_h = 1;
+    cp.h_out = h->hbuf[0];
+    rc = launch_cell<T>(h, cp, st);
+    if (rc) return rc;
+  }
+  const int n_prefix_total = n_prefix_ids + npre;  // GRU inputs before the rollout
+  for (int j = 1; j < n_prefix_total; ++j) {
+    GemvParams p = base_params(h);
+    p.nseg = 1;
+    p.seg[0] = {3 * c.gru_hidden, 0, EPI_GH};
+    p.K = c.gru_hidden;
+    p.N = h->N1;
+    p.n_valid = c.batch;
+    p.gh_out = h->ghbuf;
+    p.b_hh = h->w.b_hh;
+    rc = launch_gemv<T, PH_GH>(h, h->tm_whh, nullptr, h->tm_h[cur], p, PhaseClass::Small, true, st);
+    if (rc) return rc;
+    CellParams cp;
+    memset(&cp, 0, sizeof(cp));
+    if (j < n_prefix_ids) {
+      cp.src = 0;
+      cp.ids = ids;
+      cp.ids_ld = ids_ld;
+      cp.ids_col = j;
+    } else {
+      cp.src = 1;
+      cp.slots = h->slots;
+      cp.nslots = h->nslots;
+      cp.slot_idx = j - n_prefix_ids;
+      cp.out = prefix_out;
+      cp.out_ld = out_ld;
+      cp.out_col = j;
+    }
+    cp.write_h = 1;
+    cp.gh = h->ghbuf;
+    cp.h_in = h->hbuf[cur];
+    cp.h_out = h->hbuf[cur ^ 1];
+    rc = launch_cell<T>(h, cp, st);
+    if (rc) return rc;
+    cur ^= 1;
+  }
+  for (int t = 0; t < c.steps; ++t) {
+    const bool last = t + 1 == c.steps;
+    {
+      GemvParams p = base_params(h);
+      p.nseg = last ? 1 : 2;
+      p.seg[0] = {c.emb_dim, 0, EPI_SPROJ_MID};
+      p.seg[1] = {3 * c.gru_hidden, 0, EPI_GH};
+      p.K = c.gru_hidden;
+      p.N = h->N1;
+      p.n_valid = c.batch;
+      p.t = t;
+      p.z_src = h->zbuf;
+      p.z_rows_per_b = positions;
+      p.z_pos_off = npre;
+      p.mid_out = h->midbuf;
+      p.gh_out = h->ghbuf;
+      p.b_hh = h->w.b_hh;
+      rc = launch_gemv<T, PH_SGH>(h, h->tm_ws, last ? nullptr : &h->tm_whh, h->tm_h[cur], p, PhaseClass::Small, true, st);
+      if (rc) return rc;
+    }
+    {
+      GemvParams p = base_params(h);
+      p.nseg = 1;
+      p.seg[0] = {c.vocab, 0, EPI_FC2_ARGMAX};
+      p.K = c.emb_dim;
+      p.N = h->N2;
+      p.n_valid = 2 * c.batch;
+      p.t = t;
+      p.npre = npre;
+      p.base_src = base;
+      p.base_rows_per_b = positions;
+      p.base_pos_off = npre;
+      p.fc2_bias = h->w.fc2_bias;
+      rc = launch_gemv<T, PH_FC2>(h, h->tm_fc2, nullptr, h->tm_mid, p, PhaseClass::Big, true, st);
+      if (rc) return rc;
+    }
+    {
+      CellParams cp;
+      memset(&cp, 0, sizeof(cp));
+      cp.src = 1;
+      cp.slots = h->slots;
+      cp.nslots = h->nslots;
+      cp.slot_idx = npre + t;
+      cp.out = out;
+      cp.out_ld = out_ld;
+      cp.out_col = out_col0 + t;
+      cp.write_h = last ? 0 : 1;
+      cp.gh = h->ghbuf;
+      cp.h_in = h->hbuf[cur];
+      cp.h_out = h->hbuf[cur ^ 1];
+      rc = launch_cell<T>(h, cp, st);
+      if (rc) return rc;
+      cur ^= 1;
+    }
+  }
+  return DD_OK;
+}
+
+// The library links its own (static) CUDA runtime, whose current device is
+// private to it: every entry point selects the handle's device itself.
+int use_device(dd_handle* h) {
+  DD_CUDA(h, cudaSetDevice(h->device));
+  return DD_OK;
+}
+
+int check_ready(dd_handle* h) {
+  if (!h) return DD_EINVAL;
+  if (!h->have_weights) return fail(h, DD_EINVAL, "dd_set_weights has not been called");
+  if (!h->w.table) return fail(h, DD_EINVAL, "weights.table is null (build it with dd_build_table)");
+  return use_device(h);
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+
+extern "C" {
+
+const char* dd_version(void) { return "domino_b200 0.1 (sm_100a, tcgen05 weight streaming)"; }
+
+int dd_create(const dd_config* cfg, int device, dd_handle** out) {
+  if (!cfg || !out) return fail(nullptr, DD_EINVAL, "null argument");
+  *out = nullptr;
+  const dd_config& c = *cfg;
+  if (c.batch < 1 || c.batch > kMaxBatch)
+    return fail(nullptr, DD_EINVAL, "batch %d outside [1, %d] (shard larger batches across handles)", c.batch,
+                kMaxBatch);
+  if (c.steps < 1 || c.hidden < 8 || c.gru_hidden < 8 || c.emb_dim < 8 || c.vocab < 2 || c.prefix_tokens < 1)
+    return fail(nullptr, DD_EINVAL, "bad shape");
+  if (c.hidden % 8 || c.gru_hidden % 8 || c.emb_dim % 8)
+    return fail(nullptr, DD_EINVAL, "hidden, gru_hidden and emb_dim must be multiples of 8");
+  if (c.dtype != DD_BF16 && c.dtype != DD_FP16) return fail(nullptr, DD_EINVAL, "dtype must be DD_BF16 or DD_FP16");
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+    return fail(nullptr, DD_ECUDA, "cannot query device %d", device);
+  if (prop.major != 10)
+    return fail(nullptr, DD_EUNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                prop.major, prop.minor);
+  dd_handle* h = new dd_handle();
+  h->device = device;
+  h->cfg = c;
+  h->num_sms = prop.multiProcessorCount;
+  h->N1 = round_up(c.batch, 16);
+  h->N2 = round_up(2 * c.batch, 16);
+  const int npre_max = c.prefix_tokens - 1;
+  h->nslots = npre_max + c.steps;
+  h->max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  auto cleanup_fail = [&](int code) {
+    dd_destroy(h);
+    cudaSetDevice(prev);
+    return code;
+  };
+  if (cudaSetDevice(device) != cudaSuccess) return cleanup_fail(fail(nullptr, DD_ECUDA, "cudaSetDevice failed"));
+  const size_t es = 2;
+  const size_t positions = (size_t)npre_max + c.steps;
+  struct A {
+    void** p;
+    size_t bytes;
+  } allocs[] = {
+      {&h->zbuf, (size_t)c.batch * positions * c.emb_dim * es},
+      {&h->midbuf, (size_t)h->N2 * c.emb_dim * es},
+      {&h->hbuf[0], (size_t)h->N1 * c.gru_hidden * es},
+      {&h->hbuf[1], (size_t)h->N1 * c.gru_hidden * es},
+      {&h->ghbuf, (size_t)c.batch * 3 * c.gru_hidden * es},
+      {(void**)&h->slots, (size_t)c.batch * h->nslots * 8},
+      {(void**)&h->partials, (size_t)2 * h->num_sms * 256 * kTileM * 4},
+      {(void**)&h->counters, (size_t)h->max_tiles * 4},
+      {(void**)&h->status, 64},
+  };
+  for (auto& a : allocs) {
+    if (cudaMalloc(a.p, a.bytes) != cudaSuccess)
+      return cleanup_fail(fail(nullptr, DD_ECUDA, "cudaMalloc(%zu) failed", a.bytes));
+    if (cudaMemset(*a.p, 0, a.bytes) != cudaSuccess)
+      return cleanup_fail(fail(nullptr, DD_ECUDA, "cudaMemset failed"));
+  }
+  int rc = encode_kmajor(h, &h->tm_mid, h->midbuf, c.dtype, c.emb_dim, h->N2, c.emb_dim, h->N2);
+  if (!rc) rc = encode_kmajor(h, &h->tm_h[0], h->hbuf[0], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
+  if (!rc) rc = encode_kmajor(h, &h->tm_h[1], h->hbuf[1], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
+  if (rc) {
+    snprintf(g_global_error, sizeof(g_global_error), "%s", h->err);
+    return cleanup_fail(rc);
+  }
+  cudaSetDevice(prev);
+  *out = h;
+  return DD_OK;
+}
+
+int dd_set_weights(dd_handle* h, const dd_weights* w) {
+  if (!h || !w) return DD_EINVAL;
+  const dd_config& c = h->cfg;
+  if (!w->fc1 || !w->fc2 || !w->w_hh) return fail(h, DD_EINVAL, "fc1, fc2 and w_hh are required");
+  if (w->fc1_ld < c.hidden + c.gru_hidden || w->fc2_ld < c.emb_dim || w->w_hh_ld < c.gru_hidden)
+    return fail(h, DD_EINVAL, "leading dimension smaller than the row length");
+  if (w->table) {
+    if (w->table_ld < 3LL * c.gru_hidden || (w->table_ld % 8) != 0 || (reinterpret_cast<uintptr_t>(w->table) & 15))
+      return fail(h, DD_EINVAL, "table must be [V, 3G], 16-byte aligned, row stride a multiple of 8 elements");
+  }
+  const char* esz = reinterpret_cast<const char*>(w->fc1);
+  int rc = encode_kmajor(h, &h->tm_wz, w->fc1, c.dtype, c.hidden, c.emb_dim, w->fc1_ld, kTileM);
+  if (!rc) rc = encode_kmajor(h, &h->tm_ws, esz + (size_t)c.hidden * 2, c.dtype, c.gru_hidden, c.emb_dim, w->fc1_ld, kTileM);
+  if (!rc) rc = encode_kmajor(h, &h->tm_fc2, w->fc2, c.dtype, c.emb_dim, c.vocab, w->fc2_ld, kTileM);
+  if (!rc) rc = encode_kmajor(h, &h->tm_whh, w->w_hh, c.dtype, c.gru_hidden, 3LL * c.gru_hidden, w->w_hh_ld, kTileM);
+  if (!rc && w->lm_head) rc = encode_kmajor(h, &h->tm_lm, w->lm_head, c.dtype, c.hidden, c.vocab, w->lm_head_ld, kTileM);
+  if (rc) return rc;
+  h->w = *w;
+  h->have_weights = true;
+  return DD_OK;
+}
+
+int dd_build_table(dd_handle* h, const void* embed, int64_t embed_ld, const void* w_ih, int64_t w_ih_ld,
+                   const void* b_ih, void* table_out, void* stream) {
+  if (!h) return DD_EINVAL;
+  const dd_config& c = h->cfg;
+  if (!embed || !w_ih || !table_out) return fail(h, DD_EINVAL, "null argument");
+  if (reinterpret_cast<uintptr_t>(table_out) & 15) return fail(h, DD_EINVAL, "table_out is not 16-byte aligned");
+  int rc = use_device(h);
+  if (rc) return rc;
+  CUtensorMap tm_wih, tm_emb;
+  rc = encode_kmajor(h, &tm_wih, w_ih, c.dtype, c.hidden, 3LL * c.gru_hidden, w_ih_ld, kTileM);
+  if (!rc) rc = encode_kmajor(h, &tm_emb, embed, c.dtype, c.hidden, c.vocab, embed_ld, 256);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  for (int n_off = 0; n_off < c.vocab; n_off += 256) {
+    GemvParams p = base_params(h);
+    p.nseg = 1;
+    p.seg[0] = {3 * c.gru_hidden, 0, EPI_TABLE};
+    p.K = c.hidden;
+    p.N = 256;
+    p.n_off = n_off;
+    p.n_valid = std::min(256, c.vocab - n_off);
+    p.table_out = table_out;
+    p.table_ld = 3LL * c.gru_hidden;
+    p.b_ih = b_ih;
+    rc = c.dtype == DD_FP16
+             ? launch_gemv<__half, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st)
+             : launch_gemv<__nv_bfloat16, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st);
+    if (rc) return rc;
+  }
+  return DD_OK;
+}
+
+int dd_rollout(dd_handle* h, const int64_t* prefix_ids, const void* parallel_hiddens, const void* base_logits,
+               int64_t* out_tokens, void* stream) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (!prefix_ids || !parallel_hiddens || !base_logits || !out_tokens) return fail(h, DD_EINVAL, "null argument");
+  const dd_config& c = h->cfg;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  DD_CUDA(h, cudaMemsetAsync(h->slots, 0, (size_t)c.batch * h->nslots * 8, st));
+  if (c.dtype == DD_FP16) {
+    rc = run_z_phase<__half>(h, parallel_hiddens, c.steps, 0, nullptr, st);
+    if (!rc)
+      rc = run_rollout<__half>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, out_tokens,
+                               c.steps, 0, nullptr, st);
+  } else {
+    rc = run_z_phase<__nv_bfloat16>(h, parallel_hiddens, c.steps, 0, nullptr, st);
+    if (!rc)
+      rc = run_rollout<__nv_bfloat16>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits,
+                                      out_tokens, c.steps, 0, nullptr, st);
+  }
+  return rc;
+}
+
+int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel_hiddens, void* base_logits_out,
+                   int64_t* verify_out, void* stream) {
+  int rc = check_ready(h);
+  if (rc) return rc;
+  if (!h->w.lm_head) return fail(h, DD_EINVAL, "weights.lm_head is null");
+  if (!last_token || !parallel_hiddens || !base_logits_out || !verify_out) return fail(h, DD_EINVAL, "null argument");
+  const dd_config& c = h->cfg;
+  const int npre = c.prefix_tokens - 1;
+  const int positions = npre + c.steps;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  DD_CUDA(h, cudaMemsetAsync(h->slots, 0, (size_t)c.batch * h->nslots * 8, st));
+  const int ld = positions + 1;
+  if (c.dtype == DD_FP16) {
+    rc = run_z_phase<__half>(h, parallel_hiddens, positions, npre, base_logits_out, st);
+    if (!rc)
+      rc = run_rollout<__half>(h, last_token, 1, 1, npre, positions, base_logits_out, verify_out, ld, 1 + npre,
+                               verify_out, st);
+  } else {
+    rc = run_z_phase<__nv_bfloat16>(h, parallel_hiddens, positions, npre, base_logits_out, st);
+    if (!rc)
+      rc = run_rollout<__nv_bfloat16>(h, last_token, 1, 1, npre, positions, base_logits_out, verify_out, ld,
+                                      1 + npre, verify_out, st);
+  }
+  return rc;
+}
+
+int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch, int32_t k1, int32_t* accept_out,
+              int64_t* bonus_out, void* stream) {
+  if (!verify_ids || !posterior || !accept_out || !bonus_out || batch < 1 || k1 < 1)
+    return fail(nullptr, DD_EINVAL, "bad accept arguments");
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, verify_ids) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
+    return fail(nullptr, DD_EINVAL, "verify_ids is not device memory");
+  if (cudaSetDevice(attr.device) != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaSetDevice failed");
+  Launch L(dim3(ceil_div(batch, 128)), dim3(128), 0, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaLaunchKernelEx(&L.cfg, accept_kernel, verify_ids, posterior, (int)batch, (int)k1, accept_out,
+                                     bonus_out);
+  if (e != cudaSuccess) return fail(nullptr, DD_ECUDA, "accept launch: %s", cudaGetErrorString(e));
+  return DD_OK;
+}
+
+int dd_set_timing(dd_handle* h, int enable) {
+  if (!h) return DD_EINVAL;
+  h->timing = enable != 0;
+  h->n_timed = 0;
+  return DD_OK;
+}
+
+int dd_read_timing(dd_handle* h, int32_t* kinds, float* ms, int32_t max_records) {
+  if (!h || (max_records > 0 && (!kinds || !ms))) return DD_EINVAL;
+  int rc = use_device(h);
+  if (rc) return rc;
+  const int n = std::min<int>(h->n_timed, max_records);
+  for (int i = 0; i < n; ++i) {
+    DD_CUDA(h, cudaEventSynchronize(h->ev[2 * i + 1]));
+    float t = 0.0f;
+    DD_CUDA(h, cudaEventElapsedTime(&t, h->ev[2 * i], h->ev[2 * i + 1]));
+    kinds[i] = h->timed_kind[i];
+    ms[i] = t;
+  }
+  h->n_timed = 0;
+  return n;
+}
+
+int dd_get_status(dd_handle* h) {
+  if (!h) return DD_EINVAL;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(h->device);
+  unsigned int s = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(&s, h->status, 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemset(h->status, 0, 4);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(h, DD_ECUDA, "dd_get_status: %s", cudaGetErrorString(e));
+  return (int)s;
+}
+
+const char* dd_last_error(const dd_handle* h) { return h ? h->err : g_global_error; }
+
+int dd_destroy(dd_handle* h) {
+  if (!h) return DD_OK;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(h->device);
+  void* ptrs[] = {h->zbuf, h->midbuf, h->hbuf[0], h->hbuf[1], h->ghbuf, h->slots, h->partials, h->counters, h->status};
+  for (void* p : ptrs)
+    if (p) cudaFree(p);
+  for (cudaEvent_t e : h->ev)
+    if (e) cudaEventDestroy(e);
+  cudaSetDevice(prev);
+  delete h;
+  return DD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,124 @@
+// dd_cell.cuh -- the small kernels between the weight-streaming phases:
+//   cell_kernel    picks the step's token (argmax word or a given id), writes
+//                  it out, gathers gi = table[token] and runs the GRU cell
+//                  h' = (1 - z) n + z h in fp32 (code/kernel/domino.py:172-226,
+//                  with gi from the embed @ W_ih^T table, domino.py:418);
+//   accept_kernel  greedy prefix acceptance (code/dflash.py:472-485).
+#pragma once
+
+#include "dd_ptx.cuh"
+
+namespace dd {
+
+struct CellParams {
+  int B, G, V;
+  int src;                      // 0: token = ids[b * ids_ld + ids_col]; 1: token = argmax word
+  const int64_t* ids;
+  int ids_ld, ids_col;
+  const unsigned long long* slots;  // word = slots[b * nslots + slot_idx]
+  int nslots, slot_idx;
+  int64_t* out;                 // if set: out[b * out_ld + out_col] = token
+  int out_ld, out_col;
+  int h_zero;                   // h = 0 and gh = b_hh (first prefix token)
+  int write_h;
+  const void* table;            // [V, 3G], row stride table_ld
+  long long table_ld;
+  const void* gh;               // [B, 3G]
+  const void* b_hh;             // [3G] or null
+  const void* h_in;             // [>=B, G]
+  void* h_out;                  // [>=B, G]
+  unsigned int* status;
+};
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = io<T>::to_f(e[i]);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) cell_kernel(const CellParams p) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int per_row = p.G / 8;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= p.B * per_row) return;
+  const int b = idx / per_row;
+  const int g0 = (idx - b * per_row) * 8;
+
+  long long tok;
+  if (p.src == 0) {
+    tok = p.ids[(size_t)b * p.ids_ld + p.ids_col];
+  } else {
+    const unsigned long long key = p.slots[(size_t)b * p.nslots + p.slot_idx];
+    if (key == 0ull) {
+      if (g0 == 0) atomicOr(p.status, 4u /* DD_STATUS_NO_ARGMAX */);
+      tok = 0;
+    } else {
+      tok = (long long)argmax_key_index(key);
+    }
+  }
+  if (tok < 0 || tok >= p.V) {
+    if (g0 == 0) atomicOr(p.status, 2u /* DD_STATUS_BAD_TOKEN */);
+    tok = tok < 0 ? 0 : p.V - 1;
+  }
+  if (p.out && g0 == 0) p.out[(size_t)b * p.out_ld + p.out_col] = tok;
+  if (!p.write_h) return;
+
+  const int G = p.G;
+  const T* gi = reinterpret_cast<const T*>(p.table) + (size_t)tok * p.table_ld;
+  float ir[8], iz[8], in_[8], hr[8], hz[8], hn[8], h[8];
+  load8<T>(gi + g0, ir);
+  load8<T>(gi + G + g0, iz);
+  load8<T>(gi + 2 * G + g0, in_);
+  if (p.h_zero) {
+    if (p.b_hh) {
+      const T* bh = reinterpret_cast<const T*>(p.b_hh);
+      load8<T>(bh + g0, hr);
+      load8<T>(bh + G + g0, hz);
+      load8<T>(bh + 2 * G + g0, hn);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hr[i] = hz[i] = hn[i] = 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = 0.0f;
+  } else {
+    const T* ghr = reinterpret_cast<const T*>(p.gh) + (size_t)b * 3 * G;
+    load8<T>(ghr + g0, hr);
+    load8<T>(ghr + G + g0, hz);
+    load8<T>(ghr + 2 * G + g0, hn);
+    load8<T>(reinterpret_cast<const T*>(p.h_in) + (size_t)b * G + g0, h);
+  }
+  alignas(16) T outv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float r = sigmoidf_(ir[i] + hr[i]);
+    const float z = sigmoidf_(iz[i] + hz[i]);
+    const float n = 2.0f * sigmoidf_(2.0f * (in_[i] + r * hn[i])) - 1.0f;
+    outv[i] = io<T>::from_f((1.0f - z) * n + z * h[i]);
+  }
+  *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h_out) + (size_t)b * G + g0) =
+      *reinterpret_cast<const uint4*>(outv);
+}
+
+// accept[b] = number of leading draft tokens equal to the target's greedy
+// tokens: (verify[:, 1:] == posterior[:, :-1]).cumprod(1).sum(1);
+// bonus[b] = posterior[b, accept[b]].
+__global__ void __launch_bounds__(128) accept_kernel(const int64_t* verify, const int64_t* posterior, int B, int K1,
+                                                     int32_t* accept, int64_t* bonus) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int64_t* v = verify + (size_t)b * K1;
+  const int64_t* q = posterior + (size_t)b * K1;
+  int a = 0;
+  while (a < K1 - 1 && v[a + 1] == q[a]) ++a;
+  accept[b] = a;
+  bonus[b] = q[a];
+}
+
+}  // namespace dd

@@ -1,0 +1,572 @@
+// dd_gemv.cuh -- the weight-streaming tcgen05 kernel behind every contraction
+// of the draft step.
+//
+// Shape of the problem.  Each phase of the draft step multiplies one or two
+// weight matrices W [R x K] (bf16/fp16, row-major, K contiguous) by a small
+// activation matrix X [N x K] (N = batch rows, or batch x positions) and
+// hands the R x N result to an epilogue.  The weights are read exactly once
+// per phase and dominate the bytes (the draft step is HBM-bound up to
+// batch 32), so the kernel is built around keeping HBM busy:
+//
+//   * one CTA per SM (persistent), 192 threads:
+//       warp 0      TMA producer: 128x64 weight tiles (16 KB, 128B-swizzled,
+//                   L2 evict_first) + the matching 64-wide slice of X
+//                   (N x 128 B, L2 evict_last: every CTA reuses it);
+//       warp 1      TMEM allocator and the single MMA-issuing thread:
+//                   tcgen05.mma kind::f16, M = 128 weight rows, N = X rows,
+//                   K = 16 per instruction, fp32 accumulators in TMEM;
+//       warps 2..5  epilogue: tcgen05.ld the 128 x N accumulator (one weight
+//                   row per thread) and apply the phase's epilogue.
+//   * stream-K partition: the phase's (tile, 64-wide k-chunk) units are cut
+//     into gridDim.x equal contiguous ranges, so every SM streams the same
+//     number of bytes (the vocab 151936 = 128 x 1187 does not divide into
+//     148 tiles evenly; splitting along K does).  A tile whose units span
+//     several CTAs is finished by the last of them to arrive: each writes its
+//     fp32 partial to scratch, and the last sums all partials in CTA order,
+//     so the result does not depend on arrival order.
+//   * programmatic dependent launch: weights never depend on the previous
+//     kernel, so the producer issues the first ring's worth of weight loads
+//     before griddepcontrol.wait and only the activation loads after it; the
+//     kernel also triggers its dependents at once, so the next phase's CTAs
+//     sit beside this one and prefetch their own weights while this phase
+//     drains.
+//
+// Every wait is bounded (kWaitLimitNs); a timeout sets DD_STATUS_TIMEOUT,
+// unwinds all roles, drains in-flight TMA/MMA and frees TMEM.
+#pragma once
+
+#include "dd_ptx.cuh"
+
+namespace dd {
+
+enum EpiKind : int {
+  EPI_LMHEAD = 1,      // base[n, v] = acc (rounded); optional prefix argmax
+  EPI_ZPROJ = 2,       // z[n, e] = acc + fc1_bias[e] (rounded)
+  EPI_SPROJ_MID = 3,   // s = acc (rounded); mid = SiLU(z_t + s) -> (hi, lo) rows 2b, 2b+1
+  EPI_GH = 4,          // gh[b, j] = acc + b_hh[j] (rounded)
+  EPI_FC2_ARGMAX = 5,  // logit = acc(hi) + acc(lo) + fc2_bias + base_t -> atomicMax key
+  EPI_TABLE = 6,       // table[n, j] = acc + b_ih[j] (rounded)
+};
+
+constexpr int kThreads = 192;
+constexpr int kEpiWarp0 = 2;
+constexpr int kTileM = 128;
+constexpr int kChunkK = 64;
+constexpr uint32_t kATileBytes = kTileM * 128;  // 16 KB
+constexpr int kMaxStages = 8;
+constexpr int kMaxBatch = 32;
+constexpr uint32_t kSmemTail = 2048;            // barriers + flags + argmax reduction
+
+struct GemvSeg {
+  int rows;
+  int tiles;
+  int kind;
+};
+
+struct GemvParams {
+  GemvSeg seg[2];
+  int nseg;
+  int K, KC;
+  int N;             // MMA N: X rows per pass, multiple of 16, <= 256
+  int n_off;         // first X row of this pass
+  int n_valid;       // X rows of this pass that carry data (<= N)
+  long long units;   // (tile, k-chunk) units in this pass
+  int stages;
+  uint32_t stage_bytes;
+  uint32_t b_bytes;
+  int acc_slots;
+  uint32_t tmem_cols;
+  uint32_t idesc;
+  int B, t, V, E, G3;
+  // EPI_LMHEAD: base_out[(n_off+n) * V + v]; prefix argmax where (n_off+n) % kpos < npre
+  void* base_out;
+  int kpos, npre;
+  unsigned long long* slots;  // [B, nslots]: prefix i < npre, rollout step npre + t
+  int nslots;
+  // EPI_ZPROJ
+  void* z_out;
+  const void* fc1_bias;
+  // EPI_SPROJ_MID: z_src[(b * z_rows_per_b + z_pos_off + t) * E + e]
+  const void* z_src;
+  int z_rows_per_b, z_pos_off;
+  void* mid_out;
+  // EPI_GH
+  void* gh_out;
+  const void* b_hh;
+  // EPI_FC2_ARGMAX: base_src[(b * base_rows_per_b + base_pos_off + t) * V + v]
+  const void* base_src;
+  int base_rows_per_b, base_pos_off;
+  const void* fc2_bias;
+  // EPI_TABLE
+  void* table_out;
+  long long table_ld;
+  const void* b_ih;
+  // stream-K scratch, status
+  float* partials;
+  unsigned int* tile_counters;
+  unsigned int* status;
+};
+
+__device__ __forceinline__ long long unit_begin(int c, long long U, int G) { return (long long)c * U / G; }
+
+__device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
+  int c = (int)((u * G) / U);
+  if (c >= G) c = G - 1;
+  while (c + 1 < G && unit_begin(c + 1, U, G) <= u) ++c;
+  while (c > 0 && unit_begin(c, U, G) > u) --c;
+  return c;
+}
+
+// Scratch slot of CTA c's partial for tile T: each CTA owns two slots, one
+// for the tile its range starts in and one for the tile it ends in.
+__device__ __forceinline__ int partial_slot(int c, long long T, long long U, int G, int KC) {
+  return 2 * c + ((unit_begin(c, U, G) / KC == T) ? 0 : 1);
+}
+
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long k) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    unsigned long long other = __shfl_xor_sync(0xFFFFFFFFu, k, o);
+    k = other > k ? other : k;
+  }
+  return k;
+}
+
+__device__ __forceinline__ bool wait_ns(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+// Context an epilogue thread needs to read its (possibly split) accumulator.
+struct AccView {
+  uint32_t taddr;      // TMEM address of this thread's lane, column 0 of the slot
+  bool combine;        // split tile finished here: sum partials of all segments
+  int nseg, myseg, c_lo;
+  long long T;
+  const float* partials;
+  int N;
+  int r;               // row within the tile
+  long long U;
+  int G, KC;
+};
+
+// 16 accumulator columns [ch*16, ch*16+16) of this thread's row, summed over
+// the tile's segments in CTA order when the tile was split.
+__device__ __forceinline__ void acc_chunk(const AccView& a, int ch, float* v) {
+  float t[16];
+  tmem_ld16(a.taddr + ch * 16, t);
+  tmem_ld_wait();
+  if (!a.combine) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = t[j];
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+  for (int s = 0; s < a.nseg; ++s) {
+    if (s == a.myseg) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += t[j];
+    } else {
+      const int slot = partial_slot(a.c_lo + s, a.T, a.U, a.G, a.KC);
+      const float* src = a.partials + (size_t)slot * a.N * kTileM;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)(ch * 16 + j) * kTileM + a.r);
+    }
+  }
+}
+
+// Phases (one kernel instantiation each, so profiles attribute time per
+// phase); kPhase also prunes the epilogues a phase cannot use.
+enum Phase : int { PH_Z = 1, PH_ZLM = 2, PH_GH = 3, PH_SGH = 4, PH_FC2 = 5, PH_TABLE = 6 };
+
+template <int kPhase>
+__device__ __forceinline__ constexpr bool phase_has(int kind) {
+  switch (kPhase) {
+    case PH_Z: return kind == EPI_ZPROJ;
+    case PH_ZLM: return kind == EPI_ZPROJ || kind == EPI_LMHEAD;
+    case PH_GH: return kind == EPI_GH;
+    case PH_SGH: return kind == EPI_SPROJ_MID || kind == EPI_GH;
+    case PH_FC2: return kind == EPI_FC2_ARGMAX;
+    case PH_TABLE: return kind == EPI_TABLE;
+  }
+  return false;
+}
+
+template <typename T, int kPhase>
+__device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView& a, int kind, int row, bool valid,
+                                              int q, int lane, unsigned long long* red, int ept) {
+  using IO = io<T>;
+  const int nchunks = p.N / 16;
+  if ((phase_has<kPhase>(EPI_LMHEAD) || phase_has<kPhase>(EPI_ZPROJ) || phase_has<kPhase>(EPI_TABLE)) &&
+      (kind == EPI_LMHEAD || kind == EPI_ZPROJ || kind == EPI_TABLE)) {
+    float bias = 0.0f;
+    if (valid) {
+      if (kind == EPI_ZPROJ && p.fc1_bias) bias = IO::load((const T*)p.fc1_bias + row);
+      if (kind == EPI_TABLE && p.b_ih) bias = IO::load((const T*)p.b_ih + row);
+    }
+    for (int ch = 0; ch < nchunks; ++ch) {
+      float v[16];
+      acc_chunk(a, ch, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int n = ch * 16 + j;
+        if (n >= p.n_valid) break;
+        const long long gn = (long long)p.n_off + n;
+        const T val = IO::from_f(v[j] + bias);
+        if (valid) {
+          if (kind == EPI_LMHEAD)
+            ((T*)p.base_out)[gn * p.V + row] = val;
+          else if (kind == EPI_ZPROJ)
+            ((T*)p.z_out)[gn * p.E + row] = val;
+          else
+            ((T*)p.table_out)[gn * p.table_ld + row] = val;
+        }
+        if (kind == EPI_LMHEAD && p.npre > 0) {
+          const int pos = (int)(gn % p.kpos);
+          if (pos < p.npre) {  // uniform across the warp
+            const float fv = IO::to_f(val);
+            unsigned long long key = (valid && !isnan(fv)) ? argmax_key(fv, (uint32_t)row) : 0ull;
+            key = warp_max_u64(key);
+            if (lane == 0 && key) atomicMax(p.slots + (gn / p.kpos) * p.nslots + pos, key);
+          }
+        }
+      }
+    }
+    return;
+  }
+  if (phase_has<kPhase>(EPI_GH) && kind == EPI_GH) {
+    const float bias = (valid && p.b_hh) ? IO::load((const T*)p.b_hh + row) : 0.0f;
+    for (int ch = 0; ch < nchunks; ++ch) {
+      float v[16];
+      acc_chunk(a, ch, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int b = ch * 16 + j;
+        if (b < p.B && valid) ((T*)p.gh_out)[(size_t)b * p.G3 + row] = IO::from_f(v[j] + bias);
+      }
+    }
+    return;
+  }
+  if (phase_has<kPhase>(EPI_SPROJ_MID) && kind == EPI_SPROJ_MID) {
+    for (int ch = 0; ch < nchunks; ++ch) {
+      float v[16];
+      acc_chunk(a, ch, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int b = ch * 16 + j;
+        if (b < p.B && valid) {
+          const float s = IO::to_f(IO::from_f(v[j]));
+          const size_t zrow = (size_t)b * p.z_rows_per_b + p.z_pos_off + p.t;
+          const float z = IO::load((const T*)p.z_src + zrow * p.E + row);
+          const float pre = z + s;
+          const float mid = pre * sigmoidf_(pre);
+          const T hi = IO::from_f(mid);
+          const T lo = IO::from_f(mid - IO::to_f(hi));
+          ((T*)p.mid_out)[(size_t)(2 * b) * p.E + row] = hi;
+          ((T*)p.mid_out)[(size_t)(2 * b + 1) * p.E + row] = lo;
+        }
+      }
+    }
+    return;
+  }
+  if (phase_has<kPhase>(EPI_FC2_ARGMAX) && kind == EPI_FC2_ARGMAX) {
+    float vals[64];
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch)
+      if (ch < nchunks) acc_chunk(a, ch, vals + ch * 16);
+    const float bias = (valid && p.fc2_bias) ? IO::load((const T*)p.fc2_bias + row) : 0.0f;
+#pragma unroll
+    for (int b = 0; b < kMaxBatch; ++b) {
+      if (b < p.B) {
+        unsigned long long key = 0ull;
+        if (valid) {
+          const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
+          float logit = vals[2 * b] + vals[2 * b + 1];
+          logit += bias;
+          logit += IO::load((const T*)p.base_src + brow * p.V + row);
+          if (!isnan(logit)) key = argmax_key(logit, (uint32_t)row);
+        }
+        key = warp_max_u64(key);
+        if (lane == 0) red[q * kMaxBatch + b] = key;
+      }
+    }
+    named_bar_sync(1, 128);
+    if (ept < p.B) {
+      unsigned long long k = red[ept];
+#pragma unroll
+      for (int w = 1; w < 4; ++w) {
+        const unsigned long long o = red[w * kMaxBatch + ept];
+        k = o > k ? o : k;
+      }
+      if (k) atomicMax(p.slots + (size_t)ept * p.nslots + p.npre + p.t, k);
+    }
+    named_bar_sync(1, 128);
+    return;
+  }
+}
+
+template <typename T, int kPhase>
+__global__ void __launch_bounds__(kThreads, 2)
+    gemv_stream_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+                       const __grid_constant__ CUtensorMap tmB, const GemvParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* tail = ring + (size_t)p.stages * p.stage_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(tail);
+  uint64_t* empty = full + kMaxStages;
+  uint64_t* accf = empty + kMaxStages;
+  uint64_t* acce = accf + 2;
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  volatile int* fin_flag = abort_flag + 1;
+  long long* issued = reinterpret_cast<long long*>(tail + 256);
+  long long* consumed = issued + 1;
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(tail + 512);  // [4][kMaxBatch]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int G = gridDim.x;
+  const int c = blockIdx.x;
+  const long long U = p.units;
+  const long long u_begin = unit_begin(c, U, G);
+  const long long u_end = unit_begin(c + 1, U, G);
+  const int KC = p.KC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&accf[s], 1);
+      mbar_init(&acce[s], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *fin_flag = 0;
+    *issued = 0;
+    *consumed = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tmA0);
+    if (p.nseg > 1) prefetch_tmap(&tmA1);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, p.tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  // Let the next phase's CTAs launch now; they only prefetch weights until
+  // this grid has completed.
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      const long long n_my = u_end - u_begin;
+      const int pre = (int)(n_my < p.stages ? n_my : p.stages);
+      auto load_a = [&](int stage, long long u) {
+        const long long tile = u / KC;
+        const int kc = (int)(u % KC);
+        const bool s1 = tile >= p.seg[0].tiles;
+        const int row0 = (int)((s1 ? tile - p.seg[0].tiles : tile) * kTileM);
+        tma_load_2d(ring + (size_t)stage * p.stage_bytes, s1 ? &tmA1 : &tmA0, &full[stage], kc * kChunkK, row0,
+                    pol_w);
+      };
+      auto load_b = [&](int stage, long long u) {
+        const int kc = (int)(u % KC);
+        tma_load_2d(ring + (size_t)stage * p.stage_bytes + kATileBytes, &tmB, &full[stage], kc * kChunkK, p.n_off,
+                    pol_x);
+      };
+      // Weights first: they do not depend on the previous kernel.
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], kATileBytes + p.b_bytes);
+        load_a(i, u_begin + i);
+      }
+      pdl_wait_primary();
+      fence_proxy_async_global();
+      for (int i = 0; i < pre; ++i) load_b(i, u_begin + i);
+      long long it = pre;
+      for (; it < n_my; ++it) {
+        const int stage = (int)(it % p.stages);
+        const uint32_t round = (uint32_t)(it / p.stages);
+        if (!mbar_wait_bounded(&empty[stage], (round & 1u) ^ 1u, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[stage], kATileBytes + p.b_bytes);
+        load_a(stage, u_begin + it);
+        load_b(stage, u_begin + it);
+      }
+      *issued = it;
+    }
+  } else if (warp == 1) {
+    pdl_wait_primary();
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      long long u = u_begin;
+      long long it = 0;
+      int acc_it = 0;
+      bool ok = true;
+      while (ok && u < u_end) {
+        const long long tile = u / KC;
+        const int kc0 = (int)(u % KC);
+        const long long left = u_end - u;
+        const int kc1 = (int)((KC - kc0) < left ? KC : kc0 + left);
+        const int slot = acc_it % p.acc_slots;
+        const uint32_t use = (uint32_t)(acc_it / p.acc_slots);
+        if (!mbar_wait_bounded(&acce[slot], (use & 1u) ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + (uint32_t)(slot * p.N);
+        for (int kc = kc0; kc < kc1; ++kc, ++it) {
+          const int stage = (int)(it % p.stages);
+          const uint32_t round = (uint32_t)(it / p.stages);
+          if (!mbar_wait_bounded(&full[stage], round & 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + (size_t)stage * p.stage_bytes);
+          const uint64_t adesc = smem_desc_k_sw128(a_addr);
+          const uint64_t bdesc = smem_desc_k_sw128(a_addr + kATileBytes);
+#pragma unroll
+          for (int k = 0; k < kChunkK / 16; ++k)
+            mma_f16_ss(d, adesc + 2 * k, bdesc + 2 * k, p.idesc, (kc > kc0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty[stage]);
+        }
+        if (!ok) break;
+        mma_commit(&accf[slot]);
+        ++acc_it;
+        u += kc1 - kc0;
+        (void)tile;
+      }
+      *consumed = it;
+    }
+  } else {
+    // -------------------------------------------------- epilogue (warps 2..5)
+    pdl_wait_primary();
+    const int ept = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    const int q = warp & 3;                         // TMEM lane quadrant of this warp
+    const int r = q * 32 + lane;                    // row within the tile
+    long long u = u_begin;
+    int acc_it = 0;
+    while (u < u_end) {
+      const long long tile = u / KC;
+      const int kc0 = (int)(u % KC);
+      const long long left = u_end - u;
+      const int kc1 = (int)((KC - kc0) < left ? KC : kc0 + left);
+      const int slot = acc_it % p.acc_slots;
+      const uint32_t use = (uint32_t)(acc_it / p.acc_slots);
+      const bool got = mbar_wait_bounded(&accf[slot], use & 1u, abort_flag);
+      if (!named_bar_and(1, 128, got)) break;
+      tc_fence_after();
+
+      const bool s1 = tile >= p.seg[0].tiles;
+      const GemvSeg& sg = p.seg[s1 ? 1 : 0];
+      const int row = (int)((s1 ? tile - p.seg[0].tiles : tile) * kTileM) + r;
+      const bool valid = row < sg.rows;
+
+      AccView a;
+      a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N);
+      a.combine = false;
+      a.nseg = 1;
+      a.myseg = 0;
+      a.c_lo = c;
+      a.T = tile;
+      a.partials = p.partials;
+      a.N = p.N;
+      a.r = r;
+      a.U = U;
+      a.G = G;
+      a.KC = KC;
+
+      bool finish = true;
+      if (kc0 > 0 || kc1 < KC) {
+        // Split tile: publish this CTA's partial; the last segment to arrive finishes.
+        const int c_lo = cta_of_unit(tile * KC, U, G);
+        const int c_hi = cta_of_unit(tile * KC + KC - 1, U, G);
+        a.nseg = c_hi - c_lo + 1;
+        a.myseg = c - c_lo;
+        a.c_lo = c_lo;
+        float* mine = p.partials + (size_t)partial_slot(c, tile, U, G, KC) * p.N * kTileM;
+        for (int ch = 0; ch < p.N / 16; ++ch) {
+          float v[16];
+          tmem_ld16(a.taddr + ch * 16, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) __stcg(mine + (size_t)(ch * 16 + j) * kTileM + r, v[j]);
+        }
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (ept == 0) {
+          const unsigned int old = atomicAdd(p.tile_counters + tile, 1u);
+          const int last = (old == (unsigned int)(a.nseg - 1)) ? 1 : 0;
+          if (last) {
+            p.tile_counters[tile] = 0u;  // ready for the next phase
+            __threadfence();
+          }
+          *fin_flag = last;
+        }
+        named_bar_sync(1, 128);
+        finish = *fin_flag != 0;
+        if (finish) {
+          __threadfence();
+          a.combine = true;
+        }
+      }
+      if (finish) epilogue_tile<T, kPhase>(p, a, sg.kind, row, valid, q, lane, red, ept);
+
+      tc_fence_before();
+      mbar_arrive(&acce[slot]);
+      ++acc_it;
+      u += kc1 - kc0;
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag) {
+    // Unwind after a timed-out wait: let in-flight MMAs and TMA loads land
+    // before the shared memory and TMEM are released.
+    if (warp == 1 && lane == 0) {
+      mma_commit(drain);
+      wait_ns(drain, 0, 100ull * 1000 * 1000);
+    }
+    if (warp == 0 && lane == 0) {
+      for (long long it = *consumed; it < *issued; ++it)
+        wait_ns(&full[it % p.stages], (uint32_t)((it / p.stages) & 1), 100ull * 1000 * 1000);
+    }
+    if (threadIdx.x == 0) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
+    __syncthreads();
+  }
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, p.tmem_cols);
+  }
+}
+
+}  // namespace dd

@@ -1,0 +1,285 @@
+"""Drop-in replacement for the reference's ``DraftCorrectionGraphRunner``.
+
+Same constructor and call signature as code/kernel/domino.py:245-256 and
+495-508, so it can be passed as ``graph_runner=`` to the reference's
+``DFlashDraftModel.spec_generate`` (code/dflash.py:313, 429-439).  The whole
+rollout runs as the hand-written sm_100a kernels of libdomino_draft.so
+(``dd_rollout``), captured once into a CUDA graph like the reference does;
+PyTorch only provides device memory, the stream and the graph.
+
+Additions on the same object:
+  * ``accept(verify_ids, posterior)`` -- greedy acceptance of every row
+    (code/dflash.py:472-485) -> (accept int32 [B], bonus int64 [B]);
+  * ``draft_block(last_token, parallel_hiddens)`` -- the whole draft side of a
+    block with the base-logit lm_head fused in (code/dflash.py:424-439);
+    needs ``target_model.lm_head``.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Tuple
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+__all__ = ["DraftCorrectionGraphRunner", "unwrap_correction_mlp", "DominoDraftError"]
+
+DominoDraftError = _lib.DominoDraftError
+
+
+def unwrap_correction_mlp(embed_proj: nn.Module):
+    """(fc1, middle, fc2) of ``embed_proj``; same checks as code/kernel/domino.py:15-50."""
+    if not isinstance(embed_proj, nn.Sequential):
+        raise TypeError("Graph runner requires draft_model.embed_proj to be nn.Sequential.")
+    modules = list(embed_proj.children())
+    if len(modules) < 2:
+        raise ValueError("embed_proj must contain at least two layers.")
+    if not isinstance(modules[0], nn.Linear):
+        raise ValueError("embed_proj first layer must be nn.Linear.")
+    if not isinstance(modules[-1], nn.Linear):
+        raise ValueError("embed_proj last layer must be nn.Linear.")
+    middle = nn.Sequential(*modules[1:-1]) if len(modules) > 2 else nn.Identity()
+    return modules[0], middle, modules[-1]
+
+
+def _middle_is_silu(middle: nn.Module) -> bool:
+    """The SiLU guard of code/kernel/domino.py:280-287."""
+    if isinstance(middle, nn.SiLU):
+        return True
+    return (
+        isinstance(middle, nn.Sequential)
+        and len(list(middle.children())) == 1
+        and isinstance(list(middle.children())[0], nn.SiLU)
+    )
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+_DTYPES = {torch.bfloat16: _lib.DD_BF16, torch.float16: _lib.DD_FP16}
+
+
+class DraftCorrectionGraphRunner:
+    """Greedy draft-correction rollout on B200 (drop-in for the reference runner).
+
+    Args mirror code/kernel/domino.py:245-256.  Extra keyword:
+      use_graph: capture ``dd_rollout`` into a CUDA graph at construction
+                 (default True, as the reference always does).
+    """
+
+    def __init__(
+        self,
+        draft_model: nn.Module,
+        target_model: nn.Module,
+        batch_size: int,
+        steps: int,
+        hidden_dim: int,
+        gru_hidden_dim: int,
+        vocab_size: int,
+        prefix_token_count: int,
+        device: torch.device,
+        use_graph: bool = True,
+    ):
+        self.steps = int(steps)
+        self.draft_model = draft_model
+        self.target_model = target_model
+        self.prefix_token_count = int(prefix_token_count)
+        self.gru_hidden_dim = int(gru_hidden_dim)
+        self.batch_size = int(batch_size)
+        self.hidden_dim = int(hidden_dim)
+        self.vocab_size = int(vocab_size)
+
+        fc1, self.middle, fc2 = unwrap_correction_mlp(draft_model.embed_proj)
+        expected_in = hidden_dim + gru_hidden_dim
+        if fc1.in_features != expected_in:
+            raise ValueError(
+                f"Correction MLP input dim mismatch: got {fc1.in_features}, "
+                f"expected {expected_in} = hidden_dim + gru_hidden_dim."
+            )
+        if not _middle_is_silu(self.middle):
+            raise NotImplementedError(
+                "the B200 runner fuses SiLU(z + s) into the fc2 contraction; "
+                f"embed_proj middle {self.middle!r} is not a single nn.SiLU"
+            )
+        gru = draft_model.prefix_gru
+        if gru.num_layers != 1 or gru.bidirectional:
+            raise ValueError("prefix_gru must be a single-layer unidirectional nn.GRU")
+
+        dtype = next(draft_model.parameters()).dtype
+        if dtype not in _DTYPES:
+            raise NotImplementedError(f"the B200 runner computes in bf16/fp16 weights, got {dtype}")
+        self.dtype = dtype
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("DraftCorrectionGraphRunner runs on a CUDA device (sm_100a)")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = device
+
+        # Non-owning views of the module parameters (the reference's
+        # `.detach().contiguous()` copies only when a view is non-contiguous).
+        self._fc1 = fc1.weight.detach()
+        self._fc1_bias = fc1.bias.detach().contiguous() if fc1.bias is not None else None
+        self._fc2 = fc2.weight.detach()
+        self._fc2_bias = fc2.bias.detach().contiguous() if fc2.bias is not None else None
+        self._w_ih = gru.weight_ih_l0.detach()
+        self._w_hh = gru.weight_hh_l0.detach()
+        self._b_ih = gru.bias_ih_l0.detach().contiguous() if gru.bias else None
+        self._b_hh = gru.bias_hh_l0.detach().contiguous() if gru.bias else None
+        embed = target_model.model.embed_tokens.weight.detach()
+        lm = getattr(target_model, "lm_head", None)
+        self._lm_head = lm.weight.detach() if isinstance(lm, nn.Linear) and lm.bias is None else None
+        for name in ("_fc1", "_fc2", "_w_ih", "_w_hh"):
+            t = getattr(self, name)
+            if t.stride(-1) != 1:
+                setattr(self, name, t.contiguous())
+        if embed.stride(-1) != 1:
+            embed = embed.contiguous()
+
+        self._lib = _lib.load()
+        cfg = _lib.DDConfig(
+            batch=self.batch_size, steps=self.steps, hidden=self.hidden_dim, gru_hidden=self.gru_hidden_dim,
+            emb_dim=fc1.out_features, vocab=self.vocab_size, prefix_tokens=self.prefix_token_count,
+            dtype=_DTYPES[dtype],
+        )
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(self._lib.dd_create(ctypes.byref(cfg), device.index, ctypes.byref(handle)), None, "dd_create")
+        self._h = handle
+
+        with torch.cuda.device(device):
+            stream = torch.cuda.current_stream(device)
+            # table[v] = embed[v] @ W_ih^T + b_ih (code/kernel/domino.py:322-327)
+            self._table = torch.empty(self.vocab_size, 3 * self.gru_hidden_dim, dtype=dtype, device=device)
+            _lib.check(
+                self._lib.dd_build_table(
+                    self._h, embed.data_ptr(), embed.stride(0), self._w_ih.data_ptr(), self._w_ih.stride(0),
+                    _ptr(self._b_ih), self._table.data_ptr(), stream.cuda_stream,
+                ),
+                self._h, "dd_build_table",
+            )
+            self._weights = _lib.DDWeights(
+                fc1=self._fc1.data_ptr(), fc1_ld=self._fc1.stride(0), fc1_bias=_ptr(self._fc1_bias),
+                fc2=self._fc2.data_ptr(), fc2_ld=self._fc2.stride(0), fc2_bias=_ptr(self._fc2_bias),
+                w_hh=self._w_hh.data_ptr(), w_hh_ld=self._w_hh.stride(0), b_hh=_ptr(self._b_hh),
+                table=self._table.data_ptr(), table_ld=self._table.stride(0),
+                lm_head=_ptr(self._lm_head), lm_head_ld=self._lm_head.stride(0) if self._lm_head is not None else 0,
+            )
+            _lib.check(self._lib.dd_set_weights(self._h, ctypes.byref(self._weights)), self._h, "dd_set_weights")
+
+            B, S = self.batch_size, self.steps
+            self.static_prefix_ids = torch.zeros(B, self.prefix_token_count, dtype=torch.long, device=device)
+            self.static_parallel_hiddens = torch.zeros(B, S, self.hidden_dim, dtype=dtype, device=device)
+            self.static_base_logits = torch.zeros(B, S, self.vocab_size, dtype=dtype, device=device)
+            self.static_out = torch.zeros(B, S, dtype=torch.long, device=device)
+            self._accept_out = torch.zeros(B, dtype=torch.int32, device=device)
+            self._bonus_out = torch.zeros(B, dtype=torch.long, device=device)
+
+            self.graph = None
+            if use_graph:
+                s = torch.cuda.Stream(device)
+                s.wait_stream(torch.cuda.current_stream(device))
+                with torch.cuda.stream(s):
+                    for _ in range(3):
+                        self._forward_impl()
+                torch.cuda.current_stream(device).wait_stream(s)
+                self.graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(self.graph):
+                    self._forward_impl()
+
+    # ------------------------------------------------------------------ core
+    def _forward_impl(self, stream=None):
+        """Enqueue one rollout over the static buffers (code/kernel/domino.py:374-431)."""
+        st = stream if stream is not None else torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(
+            self._lib.dd_rollout(
+                self._h, self.static_prefix_ids.data_ptr(), self.static_parallel_hiddens.data_ptr(),
+                self.static_base_logits.data_ptr(), self.static_out.data_ptr(), st,
+            ),
+            self._h, "dd_rollout",
+        )
+
+    @torch.inference_mode()
+    def __call__(self, prefix_ids: torch.Tensor, parallel_hiddens: torch.Tensor, base_logits: torch.Tensor) -> torch.Tensor:
+        """[B, 1+p] ids, [B, S, H] hiddens, [B, S, V] base logits -> [B, S] int64 draft tokens."""
+        self.static_prefix_ids.copy_(prefix_ids)
+        self.static_parallel_hiddens.copy_(parallel_hiddens)
+        self.static_base_logits.copy_(base_logits)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._forward_impl()
+        return self.static_out.clone()
+
+    # ------------------------------------------------------------ additions
+    @torch.inference_mode()
+    def accept(self, verify_ids: torch.Tensor, posterior: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Greedy acceptance of every row (code/dflash.py:472-485).
+
+        Returns ``(a, bonus)`` with ``a[b]`` = accepted draft tokens (the
+        reference records ``a + 1`` as the acceptance length) and
+        ``bonus[b] = posterior[b, a[b]]``.
+        """
+        v = verify_ids.to(self.device, torch.long).contiguous()
+        p = posterior.to(self.device, torch.long).contiguous()
+        if v.shape != p.shape or v.dim() != 2:
+            raise ValueError("verify_ids and posterior must both be [B, K+1]")
+        B, K1 = v.shape
+        acc = torch.empty(B, dtype=torch.int32, device=self.device)
+        bonus = torch.empty(B, dtype=torch.long, device=self.device)
+        _lib.check(
+            self._lib.dd_accept(v.data_ptr(), p.data_ptr(), B, K1, acc.data_ptr(), bonus.data_ptr(),
+                                torch.cuda.current_stream(self.device).cuda_stream),
+            None, "dd_accept",
+        )
+        return acc, bonus
+
+    @torch.inference_mode()
+    def draft_block(self, last_token: torch.Tensor, parallel_hiddens: torch.Tensor,
+                    base_logits_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Draft side of one block with the lm_head fused (code/dflash.py:424-439).
+
+        last_token [B] (verify_ids[:, 0]); parallel_hiddens [B, p+S, H].
+        Returns ``(verify_ids [B, p+S+1] int64, base_logits [B, p+S, V])``.
+        """
+        if self._lm_head is None:
+            raise ValueError("target_model.lm_head (bias-free nn.Linear) is required for draft_block")
+        B = self.batch_size
+        K = self.prefix_token_count - 1 + self.steps
+        ph = parallel_hiddens.to(self.device, self.dtype).contiguous()
+        if tuple(ph.shape) != (B, K, self.hidden_dim):
+            raise ValueError(f"parallel_hiddens must be [{B}, {K}, {self.hidden_dim}]")
+        last = last_token.to(self.device, torch.long).reshape(B).contiguous()
+        if base_logits_out is None:
+            base_logits_out = torch.empty(B, K, self.vocab_size, dtype=self.dtype, device=self.device)
+        verify = torch.empty(B, K + 1, dtype=torch.long, device=self.device)
+        _lib.check(
+            self._lib.dd_draft_block(self._h, last.data_ptr(), ph.data_ptr(), base_logits_out.data_ptr(),
+                                     verify.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream),
+            self._h, "dd_draft_block",
+        )
+        return verify, base_logits_out
+
+    def status(self) -> int:
+        """Synchronise and return (and clear) the device status bits (DD_STATUS_*)."""
+        return _lib.check(self._lib.dd_get_status(self._h), self._h, "dd_get_status")
+
+    @property
+    def table(self) -> torch.Tensor:
+        """The GRU input table embed @ W_ih^T + b_ih, [V, 3G]."""
+        return self._table
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self.graph = None
+            self._lib.dd_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,158 @@
+/*
+ * domino_draft.h -- C ABI of libdomino_draft.so, the B200 (sm_100a) draft step
+ * of Domino speculative decoding: GRU correction head + correction MLP +
+ * lm_head greedy argmax + greedy prefix acceptance.
+ *
+ * Conventions
+ *   - Every pointer argument named "device" is CUDA device memory on the
+ *     handle's device; nothing here allocates per call or synchronises.
+ *   - Tensors are row-major; "ld" is the row stride in elements.
+ *   - Weights are bf16 (DD_BF16) or fp16 (DD_FP16); token ids are int64.
+ *   - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL =
+ *     the legacy default stream).  Calls are asynchronous and can be
+ *     captured into a CUDA graph as long as the same pointers are replayed.
+ *   - Return value: DD_OK (0) or a negative DD_E* status; nothing throws
+ *     across the ABI.  dd_last_error() gives a one-line reason.
+ *   - A handle belongs to one device and is not thread-safe.
+ *
+ * Reference interfaces replaced (paths inside the Domino repository):
+ *   dd_create + dd_set_weights + dd_build_table
+ *       DraftCorrectionGraphRunner.__init__   code/kernel/domino.py:245-372
+ *   dd_rollout
+ *       DraftCorrectionGraphRunner.__call__   code/kernel/domino.py:495-508
+ *       (its captured body _forward_impl      code/kernel/domino.py:374-431)
+ *   dd_draft_block
+ *       base_logits = target.lm_head(parallel_hiddens) and the pure-draft
+ *       prefix argmax, code/dflash.py:424-427, followed by the runner call of
+ *       code/dflash.py:429-439
+ *   dd_accept
+ *       greedy acceptance, code/dflash.py:472-485
+ */
+#ifndef DOMINO_DRAFT_H
+#define DOMINO_DRAFT_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DD_OK 0
+#define DD_EINVAL (-1)      /* bad argument: shape, dtype, alignment, null pointer */
+#define DD_ECUDA (-2)       /* a CUDA runtime/driver call failed */
+#define DD_EDEVICE (-3)     /* a kernel reported an error (status word); see dd_get_status */
+#define DD_EUNSUPPORTED (-4) /* device is not sm_100 / feature not built */
+
+#define DD_BF16 0
+#define DD_FP16 1
+
+/* Device status bits (dd_get_status). */
+#define DD_STATUS_TIMEOUT 1u       /* a bounded wait inside a kernel gave up */
+#define DD_STATUS_BAD_TOKEN 2u     /* a token id was outside [0, vocab) and was clamped */
+#define DD_STATUS_NO_ARGMAX 4u     /* an argmax saw no finite candidate (all NaN) */
+
+typedef struct dd_handle dd_handle;
+
+/* Shapes of one runner (code/kernel/domino.py:245-256). */
+typedef struct dd_config {
+  int32_t batch;          /* B: rows per call */
+  int32_t steps;          /* S: draft tokens produced by one rollout */
+  int32_t hidden;         /* H: target hidden size (fc1 takes H+G inputs) */
+  int32_t gru_hidden;     /* G: GRU state size */
+  int32_t emb_dim;        /* E: correction-MLP width (fc1 outputs) */
+  int32_t vocab;          /* V */
+  int32_t prefix_tokens;  /* 1 + pure_draft_prefix_len */
+  int32_t dtype;          /* DD_BF16 or DD_FP16 */
+} dd_config;
+
+/* Non-owning device pointers to the head's parameters, in the reference's
+ * layouts (code/kernel/domino.py:272-327; code/dflash.py:261-274).  The
+ * pointed-to memory must outlive the handle or the next dd_set_weights. */
+typedef struct dd_weights {
+  const void* fc1;       int64_t fc1_ld;      /* [E, H+G]: W_z = fc1[:, :H], W_s = fc1[:, H:] */
+  const void* fc1_bias;                       /* [E] or NULL */
+  const void* fc2;       int64_t fc2_ld;      /* [V, E] */
+  const void* fc2_bias;                       /* [V] or NULL */
+  const void* w_hh;      int64_t w_hh_ld;     /* [3G, G], gate order (r, z, n) */
+  const void* b_hh;                           /* [3G] or NULL */
+  const void* table;     int64_t table_ld;    /* [V, 3G] = embed @ W_ih^T + b_ih (dd_build_table) */
+  const void* lm_head;   int64_t lm_head_ld;  /* [V, H] or NULL; needed by dd_draft_block only */
+} dd_weights;
+
+/* Create a handle for `device` (allocates the handle's scratch once). */
+int dd_create(const dd_config* cfg, int device, dd_handle** out);
+
+/* Point the handle at the head's weights and prepare their TMA descriptors. */
+int dd_set_weights(dd_handle* h, const dd_weights* w);
+
+/* table[v, :] = embed[v, :] @ W_ih^T + b_ih, rounded to the weight dtype
+ * (code/kernel/domino.py:322-327).  embed [V, H], w_ih [3G, H], b_ih [3G] or
+ * NULL, table_out [V, 3G] with row stride 3G. */
+int dd_build_table(dd_handle* h, const void* embed, int64_t embed_ld, const void* w_ih,
+                   int64_t w_ih_ld, const void* b_ih, void* table_out, void* stream);
+
+/* One rollout: the runner call of code/kernel/domino.py:495-508.
+ *   prefix_ids       [B, prefix_tokens] int64 (verify_ids[:, :1+p])
+ *   parallel_hiddens [B, S, H]                (hidden states of the S positions)
+ *   base_logits      [B, S, V]                (target.lm_head of those positions)
+ *   out_tokens       [B, S] int64             (greedy corrected draft tokens) */
+int dd_rollout(dd_handle* h, const int64_t* prefix_ids, const void* parallel_hiddens,
+               const void* base_logits, int64_t* out_tokens, void* stream);
+
+/* The whole draft side of one block (code/dflash.py:424-439) with the lm_head
+ * projection fused in: base = lm_head(parallel_hiddens) for all K = p + S
+ * positions, the p pure-draft prefix tokens = argmax(base[:, :p]), then the
+ * rollout over positions p..K-1.
+ *   last_token       [B] int64     (verify_ids[:, 0], the last accepted token)
+ *   parallel_hiddens [B, K, H]
+ *   base_logits_out  [B, K, V]     (written; bf16/fp16 like the weights)
+ *   verify_out       [B, K + 1] int64: (last_token, p prefix tokens, S draft tokens) */
+int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel_hiddens,
+                   void* base_logits_out, int64_t* verify_out, void* stream);
+
+/* Greedy acceptance (code/dflash.py:472-485) for every row:
+ *   verify_ids [B, K1] int64, posterior [B, K1] int64 (K1 = draft tokens + 1)
+ *   accept_out [B] int32: leading draft tokens equal to the target's
+ *   bonus_out  [B] int64: posterior[b, accept_out[b]]
+ * The reference records accept + 1 as the block's acceptance length. */
+int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch, int32_t k1,
+              int32_t* accept_out, int64_t* bonus_out, void* stream);
+
+/* Launch kinds reported by dd_read_timing. */
+#define DD_PHASE_Z 1      /* z = parallel_hiddens @ W_z^T */
+#define DD_PHASE_ZLM 2    /* the same fused with the lm_head base logits */
+#define DD_PHASE_GH 3     /* gh = h @ W_hh^T (prefix GRU) */
+#define DD_PHASE_SGH 4    /* s = h @ W_s^T -> SiLU mid, and gh = h @ W_hh^T */
+#define DD_PHASE_FC2 5    /* fc2 contraction + base logits + argmax */
+#define DD_PHASE_TABLE 6  /* embed @ W_ih^T table */
+#define DD_PHASE_CELL 7   /* token pick + GRU cell */
+
+/* Benchmarking aid (no counterpart in the reference): while enabled, the
+ * handle records a CUDA event pair around every kernel it launches on the
+ * caller's stream.  The events separate launches that otherwise overlap
+ * (programmatic dependent launch), so enable it only to time kernels. */
+int dd_set_timing(dd_handle* h, int enable);
+
+/* Synchronise, return the number n of launches recorded since timing was
+ * enabled or last read (at most max_records), their DD_PHASE_* kinds and
+ * durations in milliseconds, and clear the record. */
+int dd_read_timing(dd_handle* h, int32_t* kinds, float* ms, int32_t max_records);
+
+/* Synchronise the handle's device and return (and clear) its status word
+ * (DD_STATUS_* bits); negative on a CUDA error. */
+int dd_get_status(dd_handle* h);
+
+/* One-line reason for the last failing call on this handle (never NULL). */
+const char* dd_last_error(const dd_handle* h);
+
+/* Library version string. */
+const char* dd_version(void);
+
+/* Free the handle's scratch; does not touch the weights. */
+int dd_destroy(dd_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DOMINO_DRAFT_H */

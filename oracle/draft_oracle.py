@@ -285,6 +285,7 @@ class RolloutTrace:
     tokens: np.ndarray                    # [B, S] int64, the oracle's own argmax per step
     gaps: np.ndarray                      # [B, S] fp32 top-2 gap of the step's logits
     chosen_logit: np.ndarray              # [B, S] fp32 logit of the token fed back
+    max_logit: np.ndarray                 # [B, S] fp32 largest logit of the step
     fed_tokens: np.ndarray                # [B, S] tokens fed to the GRU (teacher or own)
     h0: np.ndarray                        # [B, G]
     h: list = field(default_factory=list)  # per step, the GRU state entering the step
@@ -321,7 +322,8 @@ def rollout(
     fed = np.zeros((B, S), np.int64)
     gaps = np.zeros((B, S), np.float32)
     chosen = np.zeros((B, S), np.float32)
-    trace = RolloutTrace(tokens, gaps, chosen, fed, h0=h.copy(), z_part=z_part)
+    top = np.zeros((B, S), np.float32)
+    trace = RolloutTrace(tokens, gaps, chosen, top, fed, h0=h.copy(), z_part=z_part)
     for t in range(S):
         trace.h.append(h.copy())
         s_proj = linear(h, w.w_s, None, dtype)                  # domino.py:397
@@ -332,6 +334,7 @@ def rollout(
         own = argmax_lowest(logits)
         tokens[:, t] = own
         gaps[:, t] = top2_gap(logits)
+        top[:, t] = logits[np.arange(B), own]
         cur = own if teacher_tokens is None else np.asarray(teacher_tokens, np.int64)[:, t]
         fed[:, t] = cur
         chosen[:, t] = logits[np.arange(B), cur]

@@ -1,0 +1,209 @@
+"""Parity of the sm_100a path (through libdomino_draft's C ABI) with the
+oracle and with the reference's own outputs (golden fixtures).
+
+Token rule: every draft token equals the oracle's argmax given the same
+history (teacher forcing), or the oracle's logit of that token is within
+2e-2 (abs + rel) of its top logit (a near-tie).  Integer outputs
+(acceptance, bonus tokens, prefix tokens over identical logits) are exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import draft_oracle as O
+from tests.fixtures import ROLLOUT_CASES, as_f32, load
+from tests.gpu_helpers import (
+    TOL, modules_from_fixture, oracle_weights, random_inputs, random_modules, teacher_forced_check,
+)
+
+pytestmark = pytest.mark.gpu
+
+cuda = pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _require_gpu():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    major, _ = torch.cuda.get_device_capability(0)
+    if major != 10:
+        pytest.fail("GPU tests need an sm_100 device")
+
+
+def make_runner(draft, target, B, S, H, G, V, P, **kw):
+    from domino_b200 import DraftCorrectionGraphRunner
+    return DraftCorrectionGraphRunner(draft, target, B, S, H, G, V, P, torch.device("cuda", 0), **kw)
+
+
+@pytest.mark.parametrize("case", [c for c in ROLLOUT_CASES if "bf16" in c])
+def test_golden_fixture_tokens(case):
+    """The reference's own tokens (Triton branch) for the fixture inputs."""
+    fx = load(case)
+    B, H, G, E, V, S, P = (int(x) for x in fx["meta"][:7])
+    draft, target = modules_from_fixture(fx)
+    r = make_runner(draft, target, B, S, H, G, V, P)
+    prefix = torch.from_numpy(fx["prefix_ids"]).cuda()
+    ph = torch.from_numpy(as_f32(fx["parallel_hiddens"])).cuda().bfloat16()
+    base = torch.from_numpy(as_f32(fx["base_logits"])).cuda().bfloat16()
+    out = r(prefix, ph, base)
+    assert r.status() == 0
+    ref = fx["tokens_triton"]
+    got = out.cpu().numpy()
+    w = oracle_weights(draft, target)
+    frac, tr = teacher_forced_check(w, prefix, ph, base, out, min_exact=0.85)
+    # Against the reference directly: where the reference's own step had a
+    # clear winner (gap >= TOL under the reference's history), we agree.
+    tr_ref = O.rollout(w, fx["prefix_ids"], as_f32(fx["parallel_hiddens"]), as_f32(fx["base_logits"]),
+                       teacher_tokens=ref)
+    first_diff = np.argmax(got != ref, axis=1)
+    for b in range(B):
+        if (got[b] == ref[b]).all():
+            continue
+        t = first_diff[b]
+        assert tr_ref.gaps[b, t] < TOL, (b, t, tr_ref.gaps[b, t])
+
+
+def test_table_matches_oracle():
+    H, G, E, V = 128, 96, 160, 1000
+    draft, target = random_modules(H, G, E, V, seed=3, gru_bias=True)
+    r = make_runner(draft, target, 2, 15, H, G, V, 1, use_graph=False)
+    w = oracle_weights(draft, target)
+    ref = w.get_table()
+    got = r.table.float().cpu().numpy()
+    assert np.all(np.abs(got - ref) <= TOL + TOL * np.abs(ref))
+    # bf16 rounding of an fp32 sum: all but a few elements are bit-identical
+    assert np.mean(got == ref) > 0.99
+
+
+SHAPES = [
+    # B, H, G, E, V, S, P, biases, fc2_std
+    (1, 256, 256, 320, 3000, 15, 1, False, 0.05),
+    (5, 256, 192, 320, 3001, 15, 1, False, 0.05),
+    (3, 128, 128, 200, 2000, 13, 3, True, 0.05),
+    (8, 128, 64, 136, 1500, 15, 1, True, 0.08),
+    (17, 64, 64, 96, 1000, 15, 2, False, 0.1),
+    (32, 128, 128, 256, 2500, 15, 1, False, 0.05),
+]
+
+
+@pytest.mark.parametrize("B,H,G,E,V,S,P,bias,fc2_std", SHAPES)
+def test_rollout_random_shapes(B, H, G, E, V, S, P, bias, fc2_std):
+    draft, target = random_modules(H, G, E, V, seed=B * 7 + H, fc2_std=fc2_std,
+                                   fc1_bias=bias, fc2_bias=bias, gru_bias=bias)
+    r = make_runner(draft, target, B, S, H, G, V, P)
+    prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=B)
+    out = r(prefix, ph, base)
+    assert r.status() == 0
+    assert out.shape == (B, S) and out.dtype == torch.long
+    teacher_forced_check(oracle_weights(draft, target), prefix, ph, base, out)
+
+
+def test_rollout_fp16():
+    B, H, G, E, V, S, P = 2, 128, 128, 192, 1200, 15, 1
+    draft, target = random_modules(H, G, E, V, seed=11, dtype=torch.float16, fc2_std=0.08)
+    r = make_runner(draft, target, B, S, H, G, V, P)
+    prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=5, dtype=torch.float16)
+    out = r(prefix, ph, base)
+    assert r.status() == 0
+    teacher_forced_check(oracle_weights(draft, target, "fp16"), prefix, ph, base, out)
+
+
+def test_graph_replay_matches_eager_and_is_deterministic():
+    B, H, G, E, V, S, P = 4, 128, 128, 256, 2048, 15, 1
+    draft, target = random_modules(H, G, E, V, seed=21, fc2_std=0.08)
+    rg = make_runner(draft, target, B, S, H, G, V, P, use_graph=True)
+    re = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    for seed in range(3):
+        prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=seed)
+        a = rg(prefix, ph, base)
+        b = re(prefix, ph, base)
+        c = rg(prefix, ph, base)
+        assert torch.equal(a, b) and torch.equal(a, c)
+
+
+def test_draft_block_fused_lm_head():
+    B, H, G, E, V, S, P = 3, 128, 128, 192, 1500, 13, 3
+    draft, target = random_modules(H, G, E, V, seed=31, fc2_std=0.08)
+    r = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    K = P - 1 + S
+    g = torch.Generator().manual_seed(9)
+    ph = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    last = torch.randint(0, V, (B,), generator=g).cuda()
+    verify, base = r.draft_block(last, ph)
+    assert r.status() == 0
+    lm = target.lm_head.weight.float().cpu().numpy()
+    base_ref = O.lm_head(ph.float().cpu().numpy(), lm, "bf16")
+    base_np = base.float().cpu().numpy()
+    assert np.all(np.abs(base_np - base_ref) <= TOL + TOL * np.abs(base_ref))
+    v = verify.cpu().numpy()
+    assert np.array_equal(v[:, 0], last.cpu().numpy())
+    # pure-draft prefix tokens are the argmax of the (bf16) base logits we wrote
+    assert np.array_equal(v[:, 1:P], O.pure_draft_prefix(base_np, P - 1))
+    # the rollout part equals the runner call fed the same inputs
+    prefix_ids = torch.from_numpy(v[:, :P]).cuda()
+    out = r(prefix_ids, ph[:, P - 1:], base[:, P - 1:])
+    assert torch.equal(out.cpu(), torch.from_numpy(v[:, P:]))
+    teacher_forced_check(oracle_weights(draft, target), prefix_ids, ph[:, P - 1:], base[:, P - 1:], out)
+
+
+def test_accept_matches_oracle_and_reference_cases():
+    from domino_b200 import DraftCorrectionGraphRunner  # noqa: F401  (loads the library)
+    from domino_b200 import _lib
+    lib = _lib.load()
+    fx = load("accept_cases")
+    rng = np.random.default_rng(0)
+    B, K1 = 64, 16
+    v = rng.integers(0, 50, (B, K1))
+    p = rng.integers(0, 50, (B, K1))
+    for b in range(B):
+        a = b % K1
+        p[b, :a] = v[b, 1:a + 1]
+    cases = [(fx["verify_ids"], fx["posterior"]), (v, p)]
+    for vv, pp in cases:
+        vt = torch.from_numpy(np.ascontiguousarray(vv)).cuda()
+        pt = torch.from_numpy(np.ascontiguousarray(pp)).cuda()
+        acc = torch.empty(vt.shape[0], dtype=torch.int32, device="cuda")
+        bonus = torch.empty(vt.shape[0], dtype=torch.long, device="cuda")
+        _lib.check(lib.dd_accept(vt.data_ptr(), pt.data_ptr(), vt.shape[0], vt.shape[1], acc.data_ptr(),
+                                 bonus.data_ptr(), torch.cuda.current_stream().cuda_stream))
+        ea, eb = O.accept(vv, pp)
+        assert np.array_equal(acc.cpu().numpy(), ea)
+        assert np.array_equal(bonus.cpu().numpy(), eb)
+    np.testing.assert_array_equal(O.accept(fx["verify_ids"], fx["posterior"])[0], fx["accept"])
+
+
+def test_bad_prefix_token_sets_status_and_is_clamped():
+    B, H, G, E, V, S, P = 2, 64, 64, 96, 700, 15, 1
+    draft, target = random_modules(H, G, E, V, seed=41)
+    r = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=1)
+    prefix[0, 0] = V + 5
+    r(prefix, ph, base)
+    from domino_b200._lib import DD_STATUS_BAD_TOKEN
+    assert r.status() & DD_STATUS_BAD_TOKEN
+    assert r.status() == 0  # reading the status clears it
+
+
+def test_spec_generate_trace_replay():
+    """Replays the runner calls recorded inside the reference's block loop."""
+    fx = load("spec_trace_partial")
+    H, V, E, G = 64, 600, 96, 64
+    draft, target = random_modules(H, G, E, V, seed=0)
+    with torch.no_grad():
+        draft.embed_proj[0].weight.copy_(torch.from_numpy(as_f32(fx["fc1"])))
+        draft.embed_proj[2].weight.copy_(torch.from_numpy(as_f32(fx["fc2"])))
+        draft.prefix_gru.weight_ih_l0.copy_(torch.from_numpy(as_f32(fx["w_ih"])))
+        draft.prefix_gru.weight_hh_l0.copy_(torch.from_numpy(as_f32(fx["w_hh"])))
+        target.model.embed_tokens.weight.copy_(torch.from_numpy(as_f32(fx["embed"])))
+    r = make_runner(draft, target, 1, 15, H, G, V, 1)
+    w = oracle_weights(draft, target)
+    for i in range(fx["runner_out"].shape[0]):
+        prefix = torch.from_numpy(fx["prefix_ids"][i]).cuda()
+        ph = torch.from_numpy(as_f32(fx["parallel_hiddens"][i])).cuda().bfloat16()
+        base = torch.from_numpy(as_f32(fx["base_logits"][i])).cuda().bfloat16()
+        out = r(prefix, ph, base)
+        # The trace ran in fp32; rounding the weights to bf16 keeps the
+        # all-zero-logit ties (lowest index wins) and the winning row.
+        teacher_forced_check(w, prefix, ph, base, out, min_exact=0.8)
+        acc, bonus = r.accept(torch.from_numpy(fx["verify_ids"][i]).cuda(), torch.from_numpy(fx["posterior"][i]).cuda())
+        assert int(acc[0]) + 1 == int(fx["acceptance_lengths"][i])
