@@ -56,6 +56,7 @@ def parse_args():
     ap.add_argument("--model", choices=sorted(MODELS), default="qwen3-8b")
     ap.add_argument("--batch", type=int, default=1, help="rows per GPU")
     ap.add_argument("--emb-dim", type=int, default=None, help="override E (correction-MLP width)")
+    ap.add_argument("--hidden", type=int, default=None, help="override H = G (small profiling cases)")
     ap.add_argument("--block", type=int, default=16)
     ap.add_argument("--prefix-len", type=int, default=0, help="pure_draft_prefix_len")
     ap.add_argument("--seed", type=int, default=0)
@@ -68,6 +69,8 @@ def shapes(args):
     m = dict(MODELS[args.model])
     if args.emb_dim:
         m["E"] = args.emb_dim
+    if args.hidden:
+        m["H"] = m["G"] = args.hidden
     S = args.block - 1 - args.prefix_len
     return m["H"], m["G"], m["E"], m["V"], S, args.prefix_len
 

@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -65,7 +66,20 @@ struct dd_handle {
   float* partials = nullptr;  // [2 * num_sms, 256, 128]
   unsigned int* counters = nullptr;
   int max_tiles = 0;
+  int max_ctas = 0;
   unsigned int* status = nullptr;
+  // Launch shape of the weight-streaming phases (tuning knobs, read from the
+  // environment at dd_create: DD_RING_KB_BIG, DD_RING_KB_SMALL,
+  // DD_MIN_SMEM_KB_BIG, DD_CTAS_PER_SM_BIG, DD_CTAS_PER_SM_SMALL).  "Big" phases stream the large
+  // matrices (fc2, lm_head + W_z, the table); "small" ones W_s / W_hh.
+  // Defaults measured on B200 (cfg: H = G = 4096, E = 12288, V = 151936):
+  // two CTAs per SM with ~100 KB rings stream fc2 at ~6.9 TB/s, against
+  // ~5.5 TB/s for one CTA per SM at any ring depth up to 216 KB.
+  int ring_kb_big = 100;
+  int ring_kb_small = 100;
+  int min_smem_kb_big = 0;
+  int ctas_per_sm_big = 2;
+  int ctas_per_sm_small = 2;
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
   // Opt-in per-launch timing (dd_set_timing): an event pair around each launch.
   static constexpr int kMaxTimed = 4096;
@@ -192,11 +206,13 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   }
   if (tiles > h->max_tiles) return fail(h, DD_EINVAL, "phase has %d tiles > %d", tiles, h->max_tiles);
   p.units = (long long)tiles * p.KC;
-  int grid = (int)std::min<long long>(h->num_sms, allow_split ? p.units : tiles);
+  const int ctas = h->num_sms * (cls == PhaseClass::Big ? h->ctas_per_sm_big : h->ctas_per_sm_small);
+  int grid = (int)std::min<long long>(ctas, allow_split ? p.units : tiles);
   if (grid < 1) grid = 1;
   p.b_bytes = (uint32_t)p.N * 128u;
   p.stage_bytes = kATileBytes + p.b_bytes;
-  const uint32_t ring_budget = p.N > 64 ? 196u * 1024u : (cls == PhaseClass::Big ? 110u * 1024u : 100u * 1024u);
+  const uint32_t ring_budget =
+      p.N > 64 ? 196u * 1024u : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
   p.stages = std::max(2, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
   p.acc_slots = p.N <= 128 ? 2 : 1;
   uint32_t cols = 32;
@@ -209,7 +225,8 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + kSmemTail;
   // Big phases reserve enough shared memory that two CTAs of the same phase
   // never share an SM, while one small-phase CTA still fits beside them.
-  if (cls == PhaseClass::Big && smem < 118 * 1024) smem = 118 * 1024;
+  if (cls == PhaseClass::Big && smem < (size_t)h->min_smem_kb_big * 1024) smem = (size_t)h->min_smem_kb_big * 1024;
+  if (smem > 227 * 1024) return fail(h, DD_EINVAL, "shared memory %zu exceeds 227 KB", smem);
   int rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
   rc = timing_begin(h, kPhase, st);
@@ -452,6 +469,18 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   const int npre_max = c.prefix_tokens - 1;
   h->nslots = npre_max + c.steps;
   h->max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
+  auto env_int = [](const char* name, int def, int lo, int hi) {
+    const char* v = getenv(name);
+    if (!v || !*v) return def;
+    const int x = atoi(v);
+    return x < lo ? lo : (x > hi ? hi : x);
+  };
+  h->ring_kb_big = env_int("DD_RING_KB_BIG", h->ring_kb_big, 36, 220);
+  h->ring_kb_small = env_int("DD_RING_KB_SMALL", h->ring_kb_small, 36, 220);
+  h->min_smem_kb_big = env_int("DD_MIN_SMEM_KB_BIG", h->min_smem_kb_big, 0, 227);
+  h->ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", h->ctas_per_sm_big, 1, 2);
+  h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", h->ctas_per_sm_small, 1, 2);
+  h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
   int prev = 0;
   cudaGetDevice(&prev);
   auto cleanup_fail = [&](int code) {
@@ -472,7 +501,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
       {&h->hbuf[1], (size_t)h->N1 * c.gru_hidden * es},
       {&h->ghbuf, (size_t)c.batch * 3 * c.gru_hidden * es},
       {(void**)&h->slots, (size_t)c.batch * h->nslots * 8},
-      {(void**)&h->partials, (size_t)2 * h->num_sms * 256 * kTileM * 4},
+      {(void**)&h->partials, (size_t)2 * h->max_ctas * 256 * kTileM * 4},
       {(void**)&h->counters, (size_t)h->max_tiles * 4},
       {(void**)&h->status, 64},
   };

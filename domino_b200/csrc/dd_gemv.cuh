@@ -8,7 +8,8 @@
 // per phase and dominate the bytes (the draft step is HBM-bound up to
 // batch 32), so the kernel is built around keeping HBM busy:
 //
-//   * one CTA per SM (persistent), 192 threads:
+//   * two CTAs per SM (persistent; measured faster than one CTA with a
+//     deeper ring), 192 threads each:
 //       warp 0      TMA producer: 128x64 weight tiles (16 KB, 128B-swizzled,
 //                   L2 evict_first) + the matching 64-wide slice of X
 //                   (N x 128 B, L2 evict_last: every CTA reuses it);
@@ -53,7 +54,7 @@ constexpr int kEpiWarp0 = 2;
 constexpr int kTileM = 128;
 constexpr int kChunkK = 64;
 constexpr uint32_t kATileBytes = kTileM * 128;  // 16 KB
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 16;
 constexpr int kMaxBatch = 32;
 constexpr uint32_t kSmemTail = 2048;            // barriers + flags + argmax reduction
 
@@ -338,9 +339,12 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* fin_flag = abort_flag + 1;
-  long long* issued = reinterpret_cast<long long*>(tail + 256);
+  // tail layout: [0, 512) barriers and flags, [512, 1024) counters, [1024, 2048) argmax reduction
+  static_assert((2 * kMaxStages + 5) * 8 + 16 <= 512, "barrier block overflows its slot");
+  static_assert(1024 + 4 * kMaxBatch * 8 <= kSmemTail, "reduction block overflows the tail");
+  long long* issued = reinterpret_cast<long long*>(tail + 512);
   long long* consumed = issued + 1;
-  unsigned long long* red = reinterpret_cast<unsigned long long*>(tail + 512);  // [4][kMaxBatch]
+  unsigned long long* red = reinterpret_cast<unsigned long long*>(tail + 1024);  // [4][kMaxBatch]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;

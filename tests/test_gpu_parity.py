@@ -131,7 +131,7 @@ def test_draft_block_fused_lm_head():
     last = torch.randint(0, V, (B,), generator=g).cuda()
     verify, base = r.draft_block(last, ph)
     assert r.status() == 0
-    lm = target.lm_head.weight.float().cpu().numpy()
+    lm = target.lm_head.weight.detach().float().cpu().numpy()
     base_ref = O.lm_head(ph.float().cpu().numpy(), lm, "bf16")
     base_np = base.float().cpu().numpy()
     assert np.all(np.abs(base_np - base_ref) <= TOL + TOL * np.abs(base_ref))
