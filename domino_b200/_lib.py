@@ -27,7 +27,7 @@ DD_STATUS_NO_ARGMAX = 4
 EXPORTS = (
     "dd_create", "dd_set_weights", "dd_build_table", "dd_rollout", "dd_draft_block",
     "dd_accept", "dd_get_status", "dd_last_error", "dd_version", "dd_destroy",
-    "dd_set_timing", "dd_read_timing",
+    "dd_set_timing", "dd_read_timing", "dd_rollout_noalloc",
 )
 PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell"}
 
@@ -84,6 +84,8 @@ def load() -> ctypes.CDLL:
         lib.dd_set_weights.argtypes = [vp, ctypes.POINTER(DDWeights)]
         lib.dd_build_table.argtypes = [vp, vp, i64, vp, i64, vp, vp, vp]
         lib.dd_rollout.argtypes = [vp, vp, vp, vp, vp, vp]
+        lib.dd_rollout_noalloc.argtypes = [ctypes.POINTER(DDConfig), ctypes.POINTER(DDWeights), ctypes.c_int,
+                                           vp, vp, vp, vp, vp]
         lib.dd_draft_block.argtypes = [vp, vp, vp, vp, vp, vp]
         lib.dd_accept.argtypes = [vp, vp, i32, i32, vp, vp, vp]
         lib.dd_get_status.argtypes = [vp]

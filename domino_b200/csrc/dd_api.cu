@@ -695,3 +695,150 @@ int dd_destroy(dd_handle* h) {
 }
 
 }  // extern "C"
+
+// ============================================================================ allocation-free rollout
+//
+// dd_rollout_noalloc: the rollout of dd_rollout for callers that cannot
+// allocate device memory -- code that runs while a CUDA graph is being
+// captured (cudaMalloc is not allowed there), a host that has handed all of
+// HBM to its own memory pool and treats any other allocation as a leak, or
+// a stateless foreign-function binding that has no place to keep a handle
+// and its buffers alive between calls.  Its scratch lives in the file-scope
+// array below instead of in cudaMalloc'd handle buffers.
+
+namespace {
+constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB
+constexpr int kNoAllocMaxDevices = 16;
+}  // namespace
+
+// One copy per device that loads this library's kernels, held until exit.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+
+struct NoAllocDevice {
+  bool ready = false;
+  unsigned char* base = nullptr;  // device address of g_noalloc_scratch on this device
+  int num_sms = 0;
+  dd_handle h;                    // launch state pointing into g_noalloc_scratch
+};
+NoAllocDevice g_noalloc[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+
+int noalloc_fail(dd_handle* h, int rc) {
+  if (h && h->err[0]) snprintf(g_global_error, sizeof(g_global_error), "%s", h->err);
+  return rc;
+}
+
+}  // namespace
+
+extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int device, const int64_t* prefix_ids,
+                                  const void* parallel_hiddens, const void* base_logits, int64_t* out_tokens,
+                                  void* stream) {
+  if (!cfg || !w || !prefix_ids || !parallel_hiddens || !base_logits || !out_tokens)
+    return fail(nullptr, DD_EINVAL, "dd_rollout_noalloc: null argument");
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return fail(nullptr, DD_EINVAL, "dd_rollout_noalloc: device %d outside [0, %d)", device, kNoAllocMaxDevices);
+  const dd_config& c = *cfg;
+  if (c.batch < 1 || c.batch > kMaxBatch || c.steps < 1 || c.hidden < 8 || c.gru_hidden < 8 || c.emb_dim < 8 ||
+      c.vocab < 2 || c.prefix_tokens < 1 || c.hidden % 8 || c.gru_hidden % 8 || c.emb_dim % 8 ||
+      (c.dtype != DD_BF16 && c.dtype != DD_FP16))
+    return fail(nullptr, DD_EINVAL, "dd_rollout_noalloc: bad config (same rules as dd_create)");
+
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDevice& d = g_noalloc[device];
+  if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cudaSetDevice failed");
+  if (!d.ready) {
+    // Once per device, with that device current: the device address of the
+    // static scratch.  (The host-side symbol is only a stand-in and must
+    // never be passed to a kernel.)
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
+      return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cannot query device %d", device);
+    if (prop.major != 10)
+      return fail(nullptr, DD_EUNSUPPORTED, "dd_rollout_noalloc: device %d is sm_%d%d, not sm_100", device,
+                  prop.major, prop.minor);
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    d.base = static_cast<unsigned char*>(p);
+    d.num_sms = prop.multiProcessorCount;
+    d.ready = true;
+  }
+
+  // Launch state for this call, laid out like dd_create's buffers.
+  dd_handle& h = d.h;
+  h.device = device;
+  h.num_sms = d.num_sms;
+  h.cfg = c;
+  h.have_weights = false;
+  h.timing = false;
+  h.n_timed = 0;
+  h.err[0] = 0;
+  h.N1 = round_up(c.batch, 16);
+  h.N2 = round_up(2 * c.batch, 16);
+  const int npre_max = c.prefix_tokens - 1;
+  h.nslots = npre_max + c.steps;
+  h.max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
+  {
+    auto env_int = [](const char* name, int def, int lo, int hi) {
+      const char* v = getenv(name);
+      if (!v || !*v) return def;
+      const int x = atoi(v);
+      return x < lo ? lo : (x > hi ? hi : x);
+    };
+    const dd_handle defaults_source{};
+    h.ring_kb_big = env_int("DD_RING_KB_BIG", defaults_source.ring_kb_big, 36, 220);
+    h.ring_kb_small = env_int("DD_RING_KB_SMALL", defaults_source.ring_kb_small, 36, 220);
+    h.min_smem_kb_big = env_int("DD_MIN_SMEM_KB_BIG", defaults_source.min_smem_kb_big, 0, 227);
+    h.ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", defaults_source.ctas_per_sm_big, 1, 2);
+    h.ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", defaults_source.ctas_per_sm_small, 1, 2);
+  }
+  h.max_ctas = h.num_sms * std::max(h.ctas_per_sm_big, h.ctas_per_sm_small);
+  // Widest accumulator any split tile of a rollout can have.
+  const int n_part = std::max(std::min(256, round_up(c.batch * c.steps, 16)), std::max(h.N1, h.N2));
+  const size_t positions = (size_t)npre_max + c.steps;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    unsigned char* p = d.base + off;
+    off = (off + bytes + 255) & ~size_t(255);
+    return p;
+  };
+  h.zbuf = take((size_t)c.batch * positions * c.emb_dim * 2);
+  h.midbuf = take((size_t)h.N2 * c.emb_dim * 2);
+  h.hbuf[0] = take((size_t)h.N1 * c.gru_hidden * 2);
+  h.hbuf[1] = take((size_t)h.N1 * c.gru_hidden * 2);
+  h.ghbuf = take((size_t)c.batch * 3 * c.gru_hidden * 2);
+  h.slots = reinterpret_cast<unsigned long long*>(take((size_t)c.batch * h.nslots * 8));
+  h.partials = reinterpret_cast<float*>(take((size_t)2 * h.max_ctas * n_part * kTileM * 4));
+  h.counters = reinterpret_cast<unsigned int*>(take((size_t)h.max_tiles * 4));
+  h.status = reinterpret_cast<unsigned int*>(take(64));
+  if (off > kNoAllocScratchBytes)
+    return fail(nullptr, DD_EINVAL,
+                "dd_rollout_noalloc: these shapes need %zu bytes of scratch; the static scratch holds %zu "
+                "(use dd_create/dd_rollout instead)",
+                off, kNoAllocScratchBytes);
+
+  // The scratch keeps the previous call's contents: clear what must start at
+  // zero (operand padding rows, split-tile counters, status).
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const struct {
+    void* p;
+    size_t n;
+  } zero[] = {{h.midbuf, (size_t)h.N2 * c.emb_dim * 2},
+              {h.hbuf[0], (size_t)h.N1 * c.gru_hidden * 2},
+              {h.hbuf[1], (size_t)h.N1 * c.gru_hidden * 2},
+              {h.counters, (size_t)h.max_tiles * 4},
+              {h.status, 64}};
+  for (const auto& z : zero)
+    if (cudaMemsetAsync(z.p, 0, z.n, st) != cudaSuccess)
+      return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cudaMemsetAsync failed");
+
+  int rc = encode_kmajor(&h, &h.tm_mid, h.midbuf, c.dtype, c.emb_dim, h.N2, c.emb_dim, h.N2);
+  if (!rc) rc = encode_kmajor(&h, &h.tm_h[0], h.hbuf[0], c.dtype, c.gru_hidden, h.N1, c.gru_hidden, h.N1);
+  if (!rc) rc = encode_kmajor(&h, &h.tm_h[1], h.hbuf[1], c.dtype, c.gru_hidden, h.N1, c.gru_hidden, h.N1);
+  if (!rc) rc = dd_set_weights(&h, w);
+  if (!rc) rc = dd_rollout(&h, prefix_ids, parallel_hiddens, base_logits, out_tokens, stream);
+  return rc ? noalloc_fail(&h, rc) : DD_OK;
+}

@@ -110,6 +110,29 @@ int dd_rollout(dd_handle* h, const int64_t* prefix_ids, const void* parallel_hid
 int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel_hiddens,
                    void* base_logits_out, int64_t* verify_out, void* stream);
 
+/* dd_rollout for callers that cannot allocate device memory (no counterpart
+ * in the reference).  Some callers cannot call cudaMalloc: code running while
+ * a CUDA graph is captured, hosts whose own pool owns all of HBM and treat any
+ * other allocation as a leak, and stateless foreign-function bindings with no
+ * place to keep a handle's buffers between calls.  This entry point takes the
+ * same inputs and outputs as dd_rollout plus the config, the weights and the
+ * device, and allocates nothing: its scratch is a 32 MiB static device array
+ * inside the library, which every GPU that loads the library holds until the
+ * process exits.
+ *   - The first call on a device looks up that array's device address; make
+ *     it before any stream capture on that device.
+ *   - Shapes whose scratch exceeds 32 MiB are rejected with DD_EINVAL and a
+ *     message (at H = G = 4096, E = 12288, V = 151936, 15 steps on 148 SMs:
+ *     batch <= 6).
+ *   - All calls share the one array and it keeps the last call's contents;
+ *     the call clears what must start at zero.  Calls whose work overlaps on
+ *     the GPU (two streams, or two host threads on one device) race on it:
+ *     order them on one stream.
+ *   - Errors are reported through dd_last_error(NULL). */
+int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int device, const int64_t* prefix_ids,
+                       const void* parallel_hiddens, const void* base_logits, int64_t* out_tokens,
+                       void* stream);
+
 /* Greedy acceptance (code/dflash.py:472-485) for every row:
  *   verify_ids [B, K1] int64, posterior [B, K1] int64 (K1 = draft tokens + 1)
  *   accept_out [B] int32: leading draft tokens equal to the target's
