@@ -54,7 +54,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--model", choices=sorted(MODELS), default="qwen3-8b")
-    ap.add_argument("--batch", type=int, default=1, help="rows per GPU")
+    ap.add_argument("--batch", type=int, default=1, help="rows per GPU (weak scaling)")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="split this many rows over the ranks instead (strong scaling)")
     ap.add_argument("--emb-dim", type=int, default=None, help="override E (correction-MLP width)")
     ap.add_argument("--hidden", type=int, default=None, help="override H = G (small profiling cases)")
     ap.add_argument("--block", type=int, default=16)
@@ -105,16 +107,22 @@ def measured_peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def committed_traffic(model, B, E):
-    """Per-launch DRAM bytes of the fc2 phase from a committed ncu summary, or None."""
-    path = os.path.join(ROOT, "profiles", "fc2_phase_traffic.json")
+def committed_traffic(model, B, H, E):
+    """Per-launch DRAM bytes of the fc2 phase from the committed ncu summary, or None.
+
+    profiles/fc2_phase_traffic.txt holds lines ``<model>:B<b>:H<h>:E<e> <bytes> ...``.
+    """
+    path = os.path.join(ROOT, "profiles", "fc2_phase_traffic.txt")
+    key = f"{model}:B{B}:H{H}:E{E}"
     try:
         with open(path) as f:
-            d = json.load(f)
-        rec = d.get(f"{model}:B{B}:E{E}")
-        return None if rec is None else float(rec["dram_bytes_per_launch"])
-    except Exception:
-        return None
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and parts[0] == key:
+                    return float(parts[1])
+    except OSError:
+        pass
+    return None
 
 
 # ---------------------------------------------------------------- clocks
@@ -216,8 +224,14 @@ def run_ours(args):
                                 device_id=device)
     from domino_b200 import DraftCorrectionGraphRunner, _lib
 
+    from domino_b200.parallel import max_over_ranks, shard_rows
+
     H, G, E, V, S, P = shapes(args)
     B = args.batch
+    if args.global_batch is not None:
+        B = shard_rows(args.global_batch, world, rank)[1]
+        if B < 1:
+            raise SystemExit(f"--global-batch {args.global_batch} leaves rank {rank} without rows")
     K = S + P
     draft, target = build_modules(H, G, E, V, device, args.seed + 17 * rank)
     runner = DraftCorrectionGraphRunner(draft, target, B, S, H, G, V, P + 1, device, use_graph=False)
@@ -327,17 +341,17 @@ def run_ours(args):
     launches_per_step = n / n_timed_blocks + 1  # + the accept kernel
     status = runner.status()
 
-    # ---- reduce over ranks: max time
-    t = torch.tensor([ms, ms_e2e], dtype=torch.float64, device=device)
+    # ---- reduce over ranks: the slowest rank's time; rows summed
+    ms, ms_e2e, status_f = max_over_ranks([ms, ms_e2e, float(status)], device=device)
+    status = int(status_f)
+    rows_total = B * world
     if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        st = torch.tensor([status], device=device)
-        dist.all_reduce(st, op=dist.ReduceOp.MAX)
-        status = int(st.item())
-    ms, ms_e2e = float(t[0]), float(t[1])
+        rt = torch.tensor([B], dtype=torch.int64, device=device)
+        dist.all_reduce(rt)
+        rows_total = int(rt.item())
 
     if rank == 0:
-        tokens = world * B * S * args.steps
+        tokens = rows_total * S * args.steps
         value = tokens / (ms / 1e3)
         e2e_value = tokens / (ms_e2e / 1e3)
         peak, peak_src = measured_peak_hbm()
@@ -346,7 +360,7 @@ def run_ours(args):
         achieved = fc2_b / (fc2_ms / 1e3) / 1e9
         step_b = algorithmic_bytes(B, H, G, E, V, S, P)
         step_ms = ms / args.steps
-        traffic = committed_traffic(args.model, B, E)
+        traffic = committed_traffic(args.model, B, H, E)
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -358,14 +372,14 @@ def run_ours(args):
             "us_per_block": round(step_ms * 1e3, 1),
             "per_gpu_value": round(value / world, 2),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong" if args.global_batch is not None else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1), "
                     "target tokens = draft tokens for the first k~U{0..15} positions",
             "config": {
                 "workload": workload_name(args, B, H, G, E, V, S, P),
-                "batch_per_gpu": B, "global_batch": world * B, "block": args.block, "seq_len": args.block,
+                "batch_per_gpu": B, "global_batch": rows_total, "block": args.block, "seq_len": args.block,
                 "parallelism": f"dp{world} (request batch sharded, no collective)",
                 "l2": "no flush: 8.7 GB of weights streamed per step, ~70x the 126 MB L2",
             },
