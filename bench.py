@@ -447,6 +447,7 @@ def cpu_baseline(args, draft, target, ph, last, budget_s):
     import numpy as np
 
     H, G, E, V, S, P = shapes(args)
+    threads = host_threads()
     w, lm = oracle_setup(draft, target, P)
     w.embed = np.zeros((1, H), np.float32)  # H is read from embed's shape; the table is given
     ph_np = ph.float().cpu().numpy()
@@ -459,17 +460,29 @@ def cpu_baseline(args, draft, target, ph, last, budget_s):
             break
     dt = time.perf_counter() - t0
     return {
-        "value": round(blocks * args.batch * S / dt, 4), "unit": "draft tokens/s", "cores": os.cpu_count(),
+        "value": round(blocks * args.batch * S / dt, 4), "unit": "draft tokens/s", "cores": threads,
         "kind": "port", "threads": "numpy BLAS, all host threads",
         "sample": f"{blocks} full block(s) of the same workload (batch {args.batch}, {S} draft tokens each) "
                   f"through oracle/draft_oracle.py in fp32 numpy, {dt:.1f} s",
     }
 
 
+def host_threads() -> int:
+    """Use every host thread for the oracle's BLAS calls (torchrun sets OMP_NUM_THREADS=1)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(n)
+    except Exception:
+        pass
+    return n
+
+
 def run_reference(args):
     world, rank, local = dist_env()
     if rank != 0:
         return
+    threads = host_threads()
     import numpy as np
     import torch
 
@@ -514,7 +527,7 @@ def run_reference(args):
         "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1)",
         "config": {"workload": workload_name(args, B, H, G, E, V, S, P), "batch_per_gpu": B,
                    "global_batch": B, "block": args.block, "parallelism": "host CPU, rank 0 only"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "draft tokens/s", "cores": os.cpu_count(),
+        "cpu_baseline": {"value": round(value, 4), "unit": "draft tokens/s", "cores": threads,
                          "kind": "port",
                          "sample": f"{n_steps} block(s) of batch {B} (of {args.steps} requested; capped at "
                                    f"~{args.cpu_budget_s:.0f} s), oracle/draft_oracle.py fp32 numpy, all host threads"},
