@@ -81,6 +81,18 @@ struct dd_handle {
   int ctas_per_sm_big = 2;
   int ctas_per_sm_small = 2;
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
+  // Vocab sharding (dd_set_vocab_shard): this rank owns vocab rows
+  // [v_off, v_off + v_local) of fc2 / lm_head; world == 1 means unsharded.
+  int v_off = 0;
+  int v_local = 0;
+  int world = 1;
+  int rank = 0;
+  unsigned long long* xbuf = nullptr;   // this rank's exchange buffer
+  size_t xbuf_bytes = 0;
+  unsigned long long* xseq = nullptr;   // call sequence number (device)
+  unsigned int* xdone = nullptr;        // per-slot finished-CTA counters
+  unsigned long long* peer[kMaxRanks] = {};
+  unsigned long long xtimeout_ns = 2000ull * 1000 * 1000;
   // Opt-in per-launch timing (dd_set_timing): an event pair around each launch.
   static constexpr int kMaxTimed = 4096;
   bool timing = false;
@@ -236,6 +248,8 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   return timing_end(h, st);
 }
 
+Exchange make_exchange(const dd_handle* h);
+
 template <typename T>
 int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
   cp.B = h->cfg.batch;
@@ -245,6 +259,8 @@ int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
   cp.table_ld = h->w.table_ld;
   cp.b_hh = h->w.b_hh;
   cp.status = h->status;
+  cp.xchg = make_exchange(h);
+  cp.xbuf = h->xbuf;
   const int threads = cp.B * (cp.G / 8);
   int rc = timing_begin(h, DD_PHASE_CELL, st);
   if (rc) return rc;
@@ -253,16 +269,50 @@ int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
   return timing_end(h, st);
 }
 
+Exchange make_exchange(const dd_handle* h) {
+  Exchange x;
+  memset(&x, 0, sizeof(x));
+  x.world = h->world;
+  x.rank = h->rank;
+  for (int j = 0; j < h->world; ++j) x.peer[j] = h->peer[j];
+  x.seq = h->xseq;
+  x.done = h->xdone;
+  x.nslots = h->nslots;
+  x.B = h->cfg.batch;
+  x.timeout_ns = h->xtimeout_ns;
+  return x;
+}
+
 GemvParams base_params(const dd_handle* h) {
   GemvParams p;
   memset(&p, 0, sizeof(p));
   p.B = h->cfg.batch;
-  p.V = h->cfg.vocab;
+  p.V = h->v_local;
   p.E = h->cfg.emb_dim;
   p.G3 = 3 * h->cfg.gru_hidden;
   p.slots = h->slots;
   p.nslots = h->nslots;
+  p.v_off = h->v_off;
+  p.base_ld = h->cfg.vocab;
+  p.base_out_ld = h->v_local;
+  p.base_voff = h->v_off;
+  p.xchg = make_exchange(h);
   return p;
+}
+
+__global__ void bump_sequence_kernel(unsigned long long* seq) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  *seq += 1ull;
+}
+
+// Start of a call on a vocab-sharded handle: a new sequence number, so that
+// the exchange flags of this call differ from every earlier call's.
+int begin_exchange(dd_handle* h, cudaStream_t st) {
+  if (h->world <= 1) return DD_OK;
+  Launch L(dim3(1), dim3(1), 0, st);
+  DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, bump_sequence_kernel, h->xseq));
+  return DD_OK;
 }
 
 // Z (+ lm_head) phase over the X = parallel_hiddens rows, in passes of <= 256 rows.
@@ -285,7 +335,11 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
     p.fc1_bias = h->w.fc1_bias;
     if (base_out) {
       p.nseg = 2;
-      p.seg[0] = {c.vocab, 0, EPI_LMHEAD};
+      p.seg[0] = {h->v_local, 0, EPI_LMHEAD};
+      if (npre > 0 && n_off + 256 >= rows) {  // last pass: the prefix argmax words are final
+        p.xslot0 = 0;
+        p.xslot1 = npre;
+      }
       p.seg[1] = {c.emb_dim, 0, EPI_ZPROJ};
       p.base_out = base_out;
       p.kpos = positions;
@@ -305,7 +359,8 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
 // argmax words (draft block); outputs to out[b * out_ld + out_col0 + t].
 template <typename T>
 int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, int npre, int positions,
-                const void* base, int64_t* out, int out_ld, int out_col0, int64_t* prefix_out, cudaStream_t st) {
+                const void* base, long long base_ld, long long base_voff, int64_t* out, int out_ld, int out_col0,
+                int64_t* prefix_out, cudaStream_t st) {
   const dd_config& c = h->cfg;
   int rc;
   int cur = 0;
@@ -385,13 +440,17 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     {
       GemvParams p = base_params(h);
       p.nseg = 1;
-      p.seg[0] = {c.vocab, 0, EPI_FC2_ARGMAX};
+      p.seg[0] = {h->v_local, 0, EPI_FC2_ARGMAX};
       p.K = c.emb_dim;
       p.N = h->N2;
       p.n_valid = 2 * c.batch;
       p.t = t;
       p.npre = npre;
       p.base_src = base;
+      p.base_ld = base_ld;
+      p.base_voff = base_voff;
+      p.xslot0 = npre + t;
+      p.xslot1 = npre + t + 1;
       p.base_rows_per_b = positions;
       p.base_pos_off = npre;
       p.fc2_bias = h->w.fc2_bias;
@@ -466,8 +525,10 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->num_sms = prop.multiProcessorCount;
   h->N1 = round_up(c.batch, 16);
   h->N2 = round_up(2 * c.batch, 16);
+  h->v_local = c.vocab;
   const int npre_max = c.prefix_tokens - 1;
   h->nslots = npre_max + c.steps;
+  h->xbuf_bytes = ((size_t)2 * h->nslots * kMaxRanks * c.batch + (size_t)2 * h->nslots * kMaxRanks) * 8;
   h->max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
   auto env_int = [](const char* name, int def, int lo, int hi) {
     const char* v = getenv(name);
@@ -504,6 +565,9 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
       {(void**)&h->partials, (size_t)2 * h->max_ctas * 256 * kTileM * 4},
       {(void**)&h->counters, (size_t)h->max_tiles * 4},
       {(void**)&h->status, 64},
+      {(void**)&h->xbuf, ((size_t)2 * h->nslots * kMaxRanks * c.batch + (size_t)2 * h->nslots * kMaxRanks) * 8},
+      {(void**)&h->xseq, 64},
+      {(void**)&h->xdone, (size_t)h->nslots * 4},
   };
   for (auto& a : allocs) {
     if (cudaMalloc(a.p, a.bytes) != cudaSuccess)
@@ -536,9 +600,10 @@ int dd_set_weights(dd_handle* h, const dd_weights* w) {
   const char* esz = reinterpret_cast<const char*>(w->fc1);
   int rc = encode_kmajor(h, &h->tm_wz, w->fc1, c.dtype, c.hidden, c.emb_dim, w->fc1_ld, kTileM);
   if (!rc) rc = encode_kmajor(h, &h->tm_ws, esz + (size_t)c.hidden * 2, c.dtype, c.gru_hidden, c.emb_dim, w->fc1_ld, kTileM);
-  if (!rc) rc = encode_kmajor(h, &h->tm_fc2, w->fc2, c.dtype, c.emb_dim, c.vocab, w->fc2_ld, kTileM);
+  if (!rc) rc = encode_kmajor(h, &h->tm_fc2, w->fc2, c.dtype, c.emb_dim, h->v_local, w->fc2_ld, kTileM);
   if (!rc) rc = encode_kmajor(h, &h->tm_whh, w->w_hh, c.dtype, c.gru_hidden, 3LL * c.gru_hidden, w->w_hh_ld, kTileM);
-  if (!rc && w->lm_head) rc = encode_kmajor(h, &h->tm_lm, w->lm_head, c.dtype, c.hidden, c.vocab, w->lm_head_ld, kTileM);
+  if (!rc && w->lm_head)
+    rc = encode_kmajor(h, &h->tm_lm, w->lm_head, c.dtype, c.hidden, h->v_local, w->lm_head_ld, kTileM);
   if (rc) return rc;
   h->w = *w;
   h->have_weights = true;
@@ -585,16 +650,20 @@ int dd_rollout(dd_handle* h, const int64_t* prefix_ids, const void* parallel_hid
   const dd_config& c = h->cfg;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   DD_CUDA(h, cudaMemsetAsync(h->slots, 0, (size_t)c.batch * h->nslots * 8, st));
+  rc = begin_exchange(h, st);
+  if (rc) return rc;
+  // base_logits rows are full-vocab rows; a vocab shard reads its own columns.
+  const long long ld = c.vocab, voff = h->v_off;
   if (c.dtype == DD_FP16) {
     rc = run_z_phase<__half>(h, parallel_hiddens, c.steps, 0, nullptr, st);
     if (!rc)
-      rc = run_rollout<__half>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, out_tokens,
-                               c.steps, 0, nullptr, st);
+      rc = run_rollout<__half>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, ld, voff,
+                               out_tokens, c.steps, 0, nullptr, st);
   } else {
     rc = run_z_phase<__nv_bfloat16>(h, parallel_hiddens, c.steps, 0, nullptr, st);
     if (!rc)
-      rc = run_rollout<__nv_bfloat16>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits,
-                                      out_tokens, c.steps, 0, nullptr, st);
+      rc = run_rollout<__nv_bfloat16>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, ld,
+                                      voff, out_tokens, c.steps, 0, nullptr, st);
   }
   return rc;
 }
@@ -610,17 +679,21 @@ int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel
   const int positions = npre + c.steps;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   DD_CUDA(h, cudaMemsetAsync(h->slots, 0, (size_t)c.batch * h->nslots * 8, st));
+  rc = begin_exchange(h, st);
+  if (rc) return rc;
   const int ld = positions + 1;
+  // base_logits_out holds this rank's vocab columns only: rows of v_local.
+  const long long bld = h->v_local;
   if (c.dtype == DD_FP16) {
     rc = run_z_phase<__half>(h, parallel_hiddens, positions, npre, base_logits_out, st);
     if (!rc)
-      rc = run_rollout<__half>(h, last_token, 1, 1, npre, positions, base_logits_out, verify_out, ld, 1 + npre,
-                               verify_out, st);
+      rc = run_rollout<__half>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out, ld,
+                               1 + npre, verify_out, st);
   } else {
     rc = run_z_phase<__nv_bfloat16>(h, parallel_hiddens, positions, npre, base_logits_out, st);
     if (!rc)
-      rc = run_rollout<__nv_bfloat16>(h, last_token, 1, 1, npre, positions, base_logits_out, verify_out, ld,
-                                      1 + npre, verify_out, st);
+      rc = run_rollout<__nv_bfloat16>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out,
+                                      ld, 1 + npre, verify_out, st);
   }
   return rc;
 }
@@ -637,6 +710,73 @@ int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch
   cudaError_t e = cudaLaunchKernelEx(&L.cfg, accept_kernel, verify_ids, posterior, (int)batch, (int)k1, accept_out,
                                      bonus_out);
   if (e != cudaSuccess) return fail(nullptr, DD_ECUDA, "accept launch: %s", cudaGetErrorString(e));
+  return DD_OK;
+}
+
+int dd_get_exchange_buffer(dd_handle* h, void** dev_ptr, uint64_t* bytes) {
+  if (!h || !dev_ptr) return DD_EINVAL;
+  *dev_ptr = h->xbuf;
+  if (bytes) *bytes = h->xbuf_bytes;
+  return DD_OK;
+}
+
+int dd_ipc_export(const void* dev_ptr, void* handle_out) {
+  if (!dev_ptr || !handle_out) return fail(nullptr, DD_EINVAL, "dd_ipc_export: null argument");
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, dev_ptr) != cudaSuccess || attr.type != cudaMemoryTypeDevice)
+    return fail(nullptr, DD_EINVAL, "dd_ipc_export: not device memory");
+  if (cudaSetDevice(attr.device) != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaSetDevice failed");
+  cudaIpcMemHandle_t ipc;
+  const cudaError_t e = cudaIpcGetMemHandle(&ipc, const_cast<void*>(dev_ptr));
+  if (e != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaIpcGetMemHandle: %s", cudaGetErrorString(e));
+  memcpy(handle_out, &ipc, sizeof(ipc));
+  return DD_OK;
+}
+
+int dd_ipc_open(int device, const void* handle_in, void** dev_ptr_out) {
+  if (!handle_in || !dev_ptr_out) return fail(nullptr, DD_EINVAL, "dd_ipc_open: null argument");
+  if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaSetDevice failed");
+  cudaIpcMemHandle_t ipc;
+  memcpy(&ipc, handle_in, sizeof(ipc));
+  const cudaError_t e = cudaIpcOpenMemHandle(dev_ptr_out, ipc, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaIpcOpenMemHandle: %s", cudaGetErrorString(e));
+  return DD_OK;
+}
+
+int dd_ipc_close(int device, void* dev_ptr) {
+  if (!dev_ptr) return DD_OK;
+  if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaSetDevice failed");
+  const cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  if (e != cudaSuccess) return fail(nullptr, DD_ECUDA, "cudaIpcCloseMemHandle: %s", cudaGetErrorString(e));
+  return DD_OK;
+}
+
+int dd_set_vocab_shard(dd_handle* h, int32_t rank, int32_t world, int64_t vocab_begin, int64_t vocab_end,
+                       void* const* peer_exchange_buffers) {
+  if (!h) return DD_EINVAL;
+  if (world < 1 || world > kMaxRanks || rank < 0 || rank >= world)
+    return fail(h, DD_EINVAL, "rank %d / world %d outside [0, %d)", rank, world, kMaxRanks);
+  if (vocab_begin < 0 || vocab_end <= vocab_begin || vocab_end > h->cfg.vocab)
+    return fail(h, DD_EINVAL, "vocab shard [%lld, %lld) outside [0, %d)", (long long)vocab_begin,
+                (long long)vocab_end, h->cfg.vocab);
+  if (world > 1 && !peer_exchange_buffers) return fail(h, DD_EINVAL, "peer exchange buffers are required");
+  for (int j = 0; j < kMaxRanks; ++j) h->peer[j] = nullptr;
+  for (int j = 0; j < world; ++j) {
+    void* pj = (world == 1 || j == rank) ? h->xbuf : peer_exchange_buffers[j];
+    if (!pj) return fail(h, DD_EINVAL, "exchange buffer of rank %d is null", j);
+    h->peer[j] = static_cast<unsigned long long*>(pj);
+  }
+  h->world = world;
+  h->rank = rank;
+  h->v_off = (int)vocab_begin;
+  h->v_local = (int)(vocab_end - vocab_begin);
+  h->have_weights = false;  // fc2 / lm_head must be given again as this rank's rows
+  return DD_OK;
+}
+
+int dd_set_exchange_timeout(dd_handle* h, uint64_t timeout_ns) {
+  if (!h || timeout_ns == 0) return DD_EINVAL;
+  h->xtimeout_ns = timeout_ns;
   return DD_OK;
 }
 
@@ -684,7 +824,8 @@ int dd_destroy(dd_handle* h) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(h->device);
-  void* ptrs[] = {h->zbuf, h->midbuf, h->hbuf[0], h->hbuf[1], h->ghbuf, h->slots, h->partials, h->counters, h->status};
+  void* ptrs[] = {h->zbuf,     h->midbuf,   h->hbuf[0], h->hbuf[1], h->ghbuf, h->slots,
+                  h->partials, h->counters, h->status,  h->xbuf,    h->xseq,  h->xdone};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   for (cudaEvent_t e : h->ev)
@@ -778,6 +919,10 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.err[0] = 0;
   h.N1 = round_up(c.batch, 16);
   h.N2 = round_up(2 * c.batch, 16);
+  h.v_off = 0;
+  h.v_local = c.vocab;  // unsharded
+  h.world = 1;
+  h.rank = 0;
   const int npre_max = c.prefix_tokens - 1;
   h.nslots = npre_max + c.steps;
   h.max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;

@@ -6,7 +6,7 @@
 //   accept_kernel  greedy prefix acceptance (code/dflash.py:472-485).
 #pragma once
 
-#include "dd_ptx.cuh"
+#include "dd_gemv.cuh"
 
 namespace dd {
 
@@ -28,7 +28,35 @@ struct CellParams {
   const void* h_in;             // [>=B, G]
   void* h_out;                  // [>=B, G]
   unsigned int* status;
+  Exchange xchg;                // world > 1: the slot's word is the max over all ranks' words
+  const unsigned long long* xbuf;  // this rank's exchange buffer
 };
+
+// Max over every rank's word for (slot, b), once all ranks have published it;
+// 0 with DD_STATUS_TIMEOUT set if some rank has not within the time limit.
+__device__ __forceinline__ unsigned long long gathered_word(const CellParams& p, int b, bool report) {
+  const Exchange& x = p.xchg;
+  const unsigned long long seq = *x.seq;
+  const int par = (int)(seq & 1ull);
+  unsigned long long best = 0ull;
+  const uint64_t t0 = globaltimer_ns();
+  for (int j = 0; j < x.world; ++j) {
+    const unsigned long long* f = p.xbuf + xchg_flag(x, par, p.slot_idx, j);
+    while (true) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+      if (v == seq) break;
+      if (globaltimer_ns() - t0 > x.timeout_ns) {
+        if (report) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
+        return best;
+      }
+      __nanosleep(64);
+    }
+    const unsigned long long w = __ldcv(p.xbuf + xchg_word(x, par, p.slot_idx, j, b));
+    best = w > best ? w : best;
+  }
+  return best;
+}
 
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
@@ -52,7 +80,8 @@ __global__ void __launch_bounds__(128) cell_kernel(const CellParams p) {
   if (p.src == 0) {
     tok = p.ids[(size_t)b * p.ids_ld + p.ids_col];
   } else {
-    const unsigned long long key = p.slots[(size_t)b * p.nslots + p.slot_idx];
+    const unsigned long long key =
+        p.xchg.world > 1 ? gathered_word(p, b, g0 == 0) : p.slots[(size_t)b * p.nslots + p.slot_idx];
     if (key == 0ull) {
       if (g0 == 0) atomicOr(p.status, 4u /* DD_STATUS_NO_ARGMAX */);
       tok = 0;

@@ -58,6 +58,32 @@ constexpr int kMaxStages = 16;
 constexpr int kMaxBatch = 32;
 constexpr uint32_t kSmemTail = 2048;            // barriers + flags + argmax reduction
 
+constexpr int kMaxRanks = 8;
+
+// Argmax-word exchange between vocab-sharded ranks (one process per GPU).
+// Every rank owns an exchange buffer in its own HBM, mapped into every
+// other rank's address space (CUDA IPC, over NVLink):
+//   words[2][nslots][world][B]  u64 argmax words, by (call parity, slot, writer)
+//   flags[2][nslots][world]     u64 = the call's sequence number once written
+// The last CTA of a launch that finishes slots [xslot0, xslot1) writes this
+// rank's words into every rank's buffer, then the flags; the next cell kernel
+// waits (bounded) for all ranks' flags of its slot and takes the max word.
+struct Exchange {
+  int world, rank;                         // world == 1: no exchange
+  unsigned long long* peer[kMaxRanks];     // exchange buffer of rank j, as mapped here
+  const unsigned long long* seq;           // sequence number of the current call (device)
+  unsigned int* done;                      // per-slot count of finished CTAs (local)
+  int nslots, B;
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ size_t xchg_word(const Exchange& x, int par, int slot, int writer, int b) {
+  return (((size_t)par * x.nslots + slot) * x.world + writer) * x.B + b;
+}
+__device__ __forceinline__ size_t xchg_flag(const Exchange& x, int par, int slot, int writer) {
+  return (size_t)2 * x.nslots * x.world * x.B + ((size_t)par * x.nslots + slot) * x.world + writer;
+}
+
 struct GemvSeg {
   int rows;
   int tiles;
@@ -106,6 +132,13 @@ struct GemvParams {
   float* partials;
   unsigned int* tile_counters;
   unsigned int* status;
+  // vocab sharding: this rank's rows are global vocab ids v_off + row; base
+  // logits rows have stride base_ld (input) / base_out_ld (output) and this
+  // rank's slice starts at column base_voff of an input row.
+  int v_off;
+  long long base_ld, base_out_ld, base_voff;
+  Exchange xchg;
+  int xslot0, xslot1;  // argmax words this launch publishes to every rank
 };
 
 __device__ __forceinline__ long long unit_begin(int c, long long U, int G) { return (long long)c * U / G; }
@@ -233,7 +266,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
         const T val = IO::from_f(v[j] + bias);
         if (valid) {
           if (kind == EPI_LMHEAD)
-            ((T*)p.base_out)[gn * p.V + row] = val;
+            ((T*)p.base_out)[gn * p.base_out_ld + row] = val;
           else if (kind == EPI_ZPROJ)
             ((T*)p.z_out)[gn * p.E + row] = val;
           else
@@ -243,7 +276,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           const int pos = (int)(gn % p.kpos);
           if (pos < p.npre) {  // uniform across the warp
             const float fv = IO::to_f(val);
-            unsigned long long key = (valid && !isnan(fv)) ? argmax_key(fv, (uint32_t)row) : 0ull;
+            unsigned long long key = (valid && !isnan(fv)) ? argmax_key(fv, (uint32_t)(p.v_off + row)) : 0ull;
             key = warp_max_u64(key);
             if (lane == 0 && key) atomicMax(p.slots + (gn / p.kpos) * p.nslots + pos, key);
           }
@@ -301,8 +334,8 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
           float logit = vals[2 * b] + vals[2 * b + 1];
           logit += bias;
-          logit += IO::load((const T*)p.base_src + brow * p.V + row);
-          if (!isnan(logit)) key = argmax_key(logit, (uint32_t)row);
+          logit += IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+          if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
         }
         key = warp_max_u64(key);
         if (lane == 0) red[q * kMaxBatch + b] = key;
@@ -320,6 +353,47 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     }
     named_bar_sync(1, 128);
     return;
+  }
+}
+
+// Called by the 128 epilogue threads of every CTA once all of its tiles are
+// finished.  The last CTA of the grid to get here sees every argmax word of
+// the launch (atomicMax, fenced) and copies them to every rank's exchange
+// buffer, then raises the flags.
+__device__ __forceinline__ void publish_words(const GemvParams& p, int ept, volatile int* flag) {
+  const Exchange& x = p.xchg;
+  named_bar_sync(1, 128);
+  if (ept == 0) {
+    __threadfence();
+    const unsigned int old = atomicAdd(x.done + p.xslot0, 1u);
+    const int last = old == gridDim.x - 1;
+    if (last) {
+      x.done[p.xslot0] = 0u;
+      __threadfence();
+    }
+    *flag = last;
+  }
+  named_bar_sync(1, 128);
+  if (!*flag) return;
+  const unsigned long long seq = *x.seq;
+  const int par = (int)(seq & 1ull);
+  const int nsl = p.xslot1 - p.xslot0;
+  const int n = x.world * nsl * x.B;
+  for (int i = ept; i < n; i += 128) {
+    const int j = i / (nsl * x.B);
+    const int rem = i - j * nsl * x.B;
+    const int slot = p.xslot0 + rem / x.B;
+    const int b = rem - (rem / x.B) * x.B;
+    const unsigned long long w = __ldcg(p.slots + (size_t)b * p.nslots + slot);
+    __stcg(x.peer[j] + xchg_word(x, par, slot, x.rank, b), w);
+  }
+  __threadfence_system();
+  named_bar_sync(1, 128);
+  for (int i = ept; i < x.world * nsl; i += 128) {
+    const int j = i / nsl;
+    const int slot = p.xslot0 + (i - j * nsl);
+    unsigned long long* f = x.peer[j] + xchg_flag(x, par, slot, x.rank);
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
   }
 }
 
@@ -548,6 +622,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_arrive(&acce[slot]);
       ++acc_it;
       u += kc1 - kc0;
+    }
+    if constexpr (kPhase == PH_FC2 || kPhase == PH_ZLM) {
+      if (p.xchg.world > 1 && p.xslot1 > p.xslot0 && !*abort_flag) publish_words(p, ept, fin_flag);
     }
   }
 

@@ -35,3 +35,14 @@ def max_over_ranks(values: Sequence[float], device=None) -> List[float]:
     t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return [float(x) for x in t.tolist()]
+
+
+def all_gather_bytes(blob: bytes) -> List[bytes]:
+    """Every rank's ``blob`` (e.g. a 64-byte CUDA IPC handle), in rank order."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return [bytes(blob)]
+    out: List[bytes] = [b""] * dist.get_world_size()
+    dist.all_gather_object(out, bytes(blob))
+    return out

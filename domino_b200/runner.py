@@ -65,9 +65,14 @@ _DTYPES = {torch.bfloat16: _lib.DD_BF16, torch.float16: _lib.DD_FP16}
 class DraftCorrectionGraphRunner:
     """Greedy draft-correction rollout on B200 (drop-in for the reference runner).
 
-    Args mirror code/kernel/domino.py:245-256.  Extra keyword:
-      use_graph: capture ``dd_rollout`` into a CUDA graph at construction
-                 (default True, as the reference always does).
+    Args mirror code/kernel/domino.py:245-256.  Extra keywords:
+      use_graph:   capture ``dd_rollout`` into a CUDA graph at construction
+                   (default True, as the reference always does).
+      vocab_shard: split fc2 and lm_head by vocab rows over the ranks of the
+                   default torch.distributed process group (one process per
+                   GPU); every rank must construct the runner with the same
+                   weights and call it with the same inputs.  The per-step
+                   argmax is combined across GPUs inside the kernels.
     """
 
     def __init__(
@@ -82,6 +87,7 @@ class DraftCorrectionGraphRunner:
         prefix_token_count: int,
         device: torch.device,
         use_graph: bool = True,
+        vocab_shard: bool = False,
     ):
         self.steps = int(steps)
         self.draft_model = draft_model
@@ -140,6 +146,17 @@ class DraftCorrectionGraphRunner:
             embed = embed.contiguous()
 
         self._lib = _lib.load()
+        self.rank, self.world, self.vocab_begin, self.vocab_end = 0, 1, 0, self.vocab_size
+        if vocab_shard:
+            import torch.distributed as dist
+            from .parallel import shard_rows
+
+            if dist.is_available() and dist.is_initialized():
+                self.rank, self.world = dist.get_rank(), dist.get_world_size()
+            if self.world > 8:
+                raise ValueError("vocab sharding supports up to 8 ranks")
+            start, count = shard_rows(self.vocab_size, self.world, self.rank)
+            self.vocab_begin, self.vocab_end = start, start + count
         cfg = _lib.DDConfig(
             batch=self.batch_size, steps=self.steps, hidden=self.hidden_dim, gru_hidden=self.gru_hidden_dim,
             emb_dim=fc1.out_features, vocab=self.vocab_size, prefix_tokens=self.prefix_token_count,
@@ -161,12 +178,19 @@ class DraftCorrectionGraphRunner:
                 ),
                 self._h, "dd_build_table",
             )
+            self._peer_ptrs = []
+            if self.world > 1:
+                self._setup_vocab_shard()
+            v0, v1 = self.vocab_begin, self.vocab_end
+            fc2_rows = self._fc2[v0:v1]
+            lm_rows = self._lm_head[v0:v1] if self._lm_head is not None else None
+            fc2_bias = self._fc2_bias[v0:v1] if self._fc2_bias is not None else None
             self._weights = _lib.DDWeights(
                 fc1=self._fc1.data_ptr(), fc1_ld=self._fc1.stride(0), fc1_bias=_ptr(self._fc1_bias),
-                fc2=self._fc2.data_ptr(), fc2_ld=self._fc2.stride(0), fc2_bias=_ptr(self._fc2_bias),
+                fc2=fc2_rows.data_ptr(), fc2_ld=fc2_rows.stride(0), fc2_bias=_ptr(fc2_bias),
                 w_hh=self._w_hh.data_ptr(), w_hh_ld=self._w_hh.stride(0), b_hh=_ptr(self._b_hh),
                 table=self._table.data_ptr(), table_ld=self._table.stride(0),
-                lm_head=_ptr(self._lm_head), lm_head_ld=self._lm_head.stride(0) if self._lm_head is not None else 0,
+                lm_head=_ptr(lm_rows), lm_head_ld=lm_rows.stride(0) if lm_rows is not None else 0,
             )
             _lib.check(self._lib.dd_set_weights(self._h, ctypes.byref(self._weights)), self._h, "dd_set_weights")
 
@@ -189,6 +213,32 @@ class DraftCorrectionGraphRunner:
                 self.graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(self.graph):
                     self._forward_impl()
+
+    def _setup_vocab_shard(self):
+        """Map every rank's exchange buffer here (CUDA IPC) and make this handle a vocab shard."""
+        import torch.distributed as dist
+
+        buf = ctypes.c_void_p()
+        _lib.check(self._lib.dd_get_exchange_buffer(self._h, ctypes.byref(buf), None), self._h, "exchange buffer")
+        blob = ctypes.create_string_buffer(64)
+        _lib.check(self._lib.dd_ipc_export(buf, blob), None, "dd_ipc_export")
+        from .parallel import all_gather_bytes
+
+        blobs = all_gather_bytes(blob.raw)
+        ptrs = (ctypes.c_void_p * self.world)()
+        for j, b in enumerate(blobs):
+            if j == self.rank:
+                ptrs[j] = buf.value
+                continue
+            p = ctypes.c_void_p()
+            _lib.check(self._lib.dd_ipc_open(self.device.index, ctypes.create_string_buffer(b, 64), ctypes.byref(p)),
+                       None, f"dd_ipc_open(rank {j})")
+            ptrs[j] = p.value
+            self._peer_ptrs.append(p.value)
+        _lib.check(self._lib.dd_set_vocab_shard(self._h, self.rank, self.world, self.vocab_begin, self.vocab_end,
+                                                ptrs), self._h, "dd_set_vocab_shard")
+        # every rank has mapped every buffer before anyone publishes into it
+        dist.barrier()
 
     # ------------------------------------------------------------------ core
     def _forward_impl(self, stream=None):
@@ -243,7 +293,8 @@ class DraftCorrectionGraphRunner:
         """Draft side of one block with the lm_head fused (code/dflash.py:424-439).
 
         last_token [B] (verify_ids[:, 0]); parallel_hiddens [B, p+S, H].
-        Returns ``(verify_ids [B, p+S+1] int64, base_logits [B, p+S, V])``.
+        Returns ``(verify_ids [B, p+S+1] int64, base_logits [B, p+S, V])``; with
+        ``vocab_shard`` the base logits hold this rank's vocab columns only.
         """
         if self._lm_head is None:
             raise ValueError("target_model.lm_head (bias-free nn.Linear) is required for draft_block")
@@ -254,7 +305,8 @@ class DraftCorrectionGraphRunner:
             raise ValueError(f"parallel_hiddens must be [{B}, {K}, {self.hidden_dim}]")
         last = last_token.to(self.device, torch.long).reshape(B).contiguous()
         if base_logits_out is None:
-            base_logits_out = torch.empty(B, K, self.vocab_size, dtype=self.dtype, device=self.device)
+            base_logits_out = torch.empty(B, K, self.vocab_end - self.vocab_begin, dtype=self.dtype,
+                                          device=self.device)
         verify = torch.empty(B, K + 1, dtype=torch.long, device=self.device)
         _lib.check(
             self._lib.dd_draft_block(self._h, last.data_ptr(), ph.data_ptr(), base_logits_out.data_ptr(),
@@ -275,6 +327,9 @@ class DraftCorrectionGraphRunner:
     def close(self):
         if getattr(self, "_h", None):
             self.graph = None
+            for p in getattr(self, "_peer_ptrs", []):
+                self._lib.dd_ipc_close(self.device.index, p)
+            self._peer_ptrs = []
             self._lib.dd_destroy(self._h)
             self._h = None
 

@@ -141,6 +141,44 @@ int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int device, co
 int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch, int32_t k1,
               int32_t* accept_out, int64_t* bonus_out, void* stream);
 
+/* ---- Vocab sharding across GPUs (one process per GPU) --------------------
+ * Each rank owns vocab rows [vocab_begin, vocab_end) of fc2 and lm_head and
+ * replicates the rest; per draft step every rank computes its (logit, index)
+ * argmax word and the fc2 kernel that finishes it writes it straight into
+ * every rank's exchange buffer over NVLink (peer stores), after which the
+ * next kernel on each rank takes the maximum over ranks.  This is the
+ * all-reduce(max) on packed (logit, index) words that BASELINE.json's
+ * north star describes, fused into the kernels (no separate collective).
+ *
+ * Setup per rank: dd_create -> dd_get_exchange_buffer -> dd_ipc_export ->
+ * (exchange the 64-byte handles between processes, e.g. all_gather) ->
+ * dd_ipc_open of every other rank's handle -> dd_set_vocab_shard ->
+ * dd_set_weights with fc2 / lm_head (/ fc2_bias) pointing at this rank's
+ * rows.  dd_rollout's base_logits stay full-vocab rows; dd_draft_block
+ * writes only this rank's columns ([B, K, vocab_end - vocab_begin]). */
+
+/* This handle's exchange buffer (device memory, for dd_ipc_export). */
+int dd_get_exchange_buffer(dd_handle* h, void** dev_ptr, uint64_t* bytes);
+
+/* cudaIpcGetMemHandle of a device allocation; handle_out receives 64 bytes. */
+int dd_ipc_export(const void* dev_ptr, void* handle_out);
+
+/* Map another process's exported allocation on `device`; close with dd_ipc_close. */
+int dd_ipc_open(int device, const void* handle_in, void** dev_ptr_out);
+int dd_ipc_close(int device, void* dev_ptr);
+
+/* Make this handle rank `rank` of `world` (<= 8) with vocab rows
+ * [vocab_begin, vocab_end); peer_exchange_buffers[j] is rank j's exchange
+ * buffer as mapped in this process (entry `rank` is ignored).  Must be
+ * followed by dd_set_weights.  world = 1 restores the unsharded handle. */
+int dd_set_vocab_shard(dd_handle* h, int32_t rank, int32_t world, int64_t vocab_begin, int64_t vocab_end,
+                       void* const* peer_exchange_buffers);
+
+/* Limit of the bounded wait for the other ranks' argmax words (default 2 s);
+ * when it runs out the step uses the words that arrived and the status word
+ * gets DD_STATUS_TIMEOUT. */
+int dd_set_exchange_timeout(dd_handle* h, uint64_t timeout_ns);
+
 /* Launch kinds reported by dd_read_timing. */
 #define DD_PHASE_Z 1      /* z = parallel_hiddens @ W_z^T */
 #define DD_PHASE_ZLM 2    /* the same fused with the lm_head base logits */

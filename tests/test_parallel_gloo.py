@@ -30,14 +30,15 @@ def _free_port():
 
 def _worker(rank, world, port, q):
     import torch.distributed as dist
-    from domino_b200.parallel import max_over_ranks, shard_rows
+    from domino_b200.parallel import all_gather_bytes, max_over_ranks, shard_rows
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         start, count = shard_rows(7, world, rank)
         mx = max_over_ranks([10.0 * (rank + 1), -rank])
-        q.put((rank, start, count, mx))
+        blobs = all_gather_bytes(bytes([rank]) * 64)
+        q.put((rank, start, count, mx, blobs))
     finally:
         dist.destroy_process_group()
 
@@ -53,6 +54,7 @@ def test_max_over_ranks_two_gloo_ranks():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert [(s, n) for _, s, n, _ in out] == [(0, 4), (4, 3)]
-    for _, _, _, mx in out:
+    assert [(s, n) for _, s, n, _, _ in out] == [(0, 4), (4, 3)]
+    for _, _, _, mx, blobs in out:
         assert mx == [20.0, 0.0]
+        assert blobs == [bytes([0]) * 64, bytes([1]) * 64]
