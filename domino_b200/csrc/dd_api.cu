@@ -310,6 +310,7 @@ __global__ void bump_sequence_kernel(unsigned long long* seq) {
 // the exchange flags of this call differ from every earlier call's.
 int begin_exchange(dd_handle* h, cudaStream_t st) {
   if (h->world <= 1) return DD_OK;
+  DD_CUDA(h, cudaMemsetAsync(h->xdone, 0, (size_t)h->nslots * 4, st));
   Launch L(dim3(1), dim3(1), 0, st);
   DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, bump_sequence_kernel, h->xseq));
   return DD_OK;

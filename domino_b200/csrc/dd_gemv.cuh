@@ -624,7 +624,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       u += kc1 - kc0;
     }
     if constexpr (kPhase == PH_FC2 || kPhase == PH_ZLM) {
-      if (p.xchg.world > 1 && p.xslot1 > p.xslot0 && !*abort_flag) publish_words(p, ept, fin_flag);
+      // All 128 threads decide together whether to publish (publish_words
+      // contains named barriers).
+      if (p.xchg.world > 1 && p.xslot1 > p.xslot0 && named_bar_and(1, 128, *abort_flag == 0))
+        publish_words(p, ept, fin_flag);
     }
   }
 

@@ -200,7 +200,8 @@ int dd_set_timing(dd_handle* h, int enable);
 int dd_read_timing(dd_handle* h, int32_t* kinds, float* ms, int32_t max_records);
 
 /* Synchronise the handle's device and return (and clear) its status word
- * (DD_STATUS_* bits); negative on a CUDA error. */
+ * (DD_STATUS_* bits); negative on a CUDA error.  After DD_STATUS_TIMEOUT the
+ * handle's scratch may be inconsistent: destroy it and create a new one. */
 int dd_get_status(dd_handle* h);
 
 /* One-line reason for the last failing call on this handle (never NULL). */
