@@ -273,12 +273,13 @@ def run_ours(args):
     for i in range(args.warmup):
         step(i % n_pool)
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    clocks = ClockSampler(local)
     if rank == 0:
         clocks.start()
         time.sleep(0.3)
+    # All ranks leave the barrier together (vocab shards wait on one another).
+    if world > 1:
+        dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     ev0.record()
