@@ -93,6 +93,10 @@ struct dd_handle {
   unsigned int* xdone = nullptr;        // per-slot finished-CTA counters
   unsigned long long* peer[kMaxRanks] = {};
   unsigned long long xtimeout_ns = 2000ull * 1000 * 1000;
+  // dd_verify_accept scratch: per-(row, position) argmax words + done counter
+  static constexpr int kMaxVerifyPositions = 64;
+  unsigned long long* vwords = nullptr;
+  unsigned int* vdone = nullptr;
   // Opt-in per-launch timing (dd_set_timing): an event pair around each launch.
   static constexpr int kMaxTimed = 4096;
   bool timing = false;
@@ -569,6 +573,8 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
       {(void**)&h->xbuf, ((size_t)2 * h->nslots * kMaxRanks * c.batch + (size_t)2 * h->nslots * kMaxRanks) * 8},
       {(void**)&h->xseq, 64},
       {(void**)&h->xdone, (size_t)h->nslots * 4},
+      {(void**)&h->vwords, (size_t)c.batch * dd_handle::kMaxVerifyPositions * 8},
+      {(void**)&h->vdone, 64},
   };
   for (auto& a : allocs) {
     if (cudaMalloc(a.p, a.bytes) != cudaSuccess)
@@ -714,6 +720,38 @@ int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch
   return DD_OK;
 }
 
+int dd_verify_accept(dd_handle* h, const void* target_logits, int32_t logits_dtype, int32_t k1,
+                     const int64_t* verify_ids, int64_t* posterior_out, int32_t* accept_out, int64_t* bonus_out,
+                     void* stream) {
+  if (!h) return DD_EINVAL;
+  if (!target_logits || !verify_ids || !posterior_out || !accept_out || !bonus_out)
+    return fail(h, DD_EINVAL, "dd_verify_accept: null argument");
+  if (k1 < 1 || k1 > dd_handle::kMaxVerifyPositions)
+    return fail(h, DD_EINVAL, "dd_verify_accept: %d positions outside [1, %d]", k1, dd_handle::kMaxVerifyPositions);
+  int rc = use_device(h);
+  if (rc) return rc;
+  const dd_config& c = h->cfg;
+  dim3 grid(ceil_div(c.vocab, kVerifyChunk), c.batch * k1);
+  Launch L(grid, dim3(kVerifyThreads), 0, reinterpret_cast<cudaStream_t>(stream));
+  cudaError_t e;
+  if (logits_dtype == DD_F32)
+    e = cudaLaunchKernelEx(&L.cfg, verify_accept_kernel<float>, static_cast<const float*>(target_logits), c.vocab,
+                           c.batch, (int)k1, verify_ids, posterior_out, accept_out, bonus_out, h->vwords, h->vdone,
+                           h->status);
+  else if (logits_dtype == DD_FP16)
+    e = cudaLaunchKernelEx(&L.cfg, verify_accept_kernel<__half>, static_cast<const __half*>(target_logits), c.vocab,
+                           c.batch, (int)k1, verify_ids, posterior_out, accept_out, bonus_out, h->vwords, h->vdone,
+                           h->status);
+  else if (logits_dtype == DD_BF16)
+    e = cudaLaunchKernelEx(&L.cfg, verify_accept_kernel<__nv_bfloat16>,
+                           static_cast<const __nv_bfloat16*>(target_logits), c.vocab, c.batch, (int)k1, verify_ids,
+                           posterior_out, accept_out, bonus_out, h->vwords, h->vdone, h->status);
+  else
+    return fail(h, DD_EINVAL, "dd_verify_accept: logits dtype %d", logits_dtype);
+  if (e != cudaSuccess) return fail(h, DD_ECUDA, "verify_accept launch: %s", cudaGetErrorString(e));
+  return DD_OK;
+}
+
 int dd_get_exchange_buffer(dd_handle* h, void** dev_ptr, uint64_t* bytes) {
   if (!h || !dev_ptr) return DD_EINVAL;
   *dev_ptr = h->xbuf;
@@ -825,8 +863,8 @@ int dd_destroy(dd_handle* h) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(h->device);
-  void* ptrs[] = {h->zbuf,     h->midbuf,   h->hbuf[0], h->hbuf[1], h->ghbuf, h->slots,
-                  h->partials, h->counters, h->status,  h->xbuf,    h->xseq,  h->xdone};
+  void* ptrs[] = {h->zbuf,     h->midbuf,   h->hbuf[0], h->hbuf[1], h->ghbuf, h->slots,  h->partials,
+                  h->counters, h->status,  h->xbuf,    h->xseq,    h->xdone, h->vwords, h->vdone};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   for (cudaEvent_t e : h->ev)

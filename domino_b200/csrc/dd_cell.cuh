@@ -150,4 +150,83 @@ __global__ void __launch_bounds__(128) accept_kernel(const int64_t* verify, cons
   bonus[b] = q[a];
 }
 
+// Greedy verify fused with acceptance (code/dflash.py:472-485):
+// posterior[b, j] = argmax_v logits[b, j, v] (lowest index on ties) and the
+// acceptance of verify[b, :] against it, in one pass over the logits.
+// Grid (chunks, B * K1): each CTA reduces one chunk of one row to a packed
+// (value, index) word and atomicMax-es it into words[row]; the last CTA to
+// finish (done counter) decodes all rows, runs the prefix match, and clears
+// the words and the counter for the next call.
+constexpr int kVerifyThreads = 256;
+constexpr int kVerifyChunk = 8192;
+
+template <typename L>
+__device__ __forceinline__ float logit_at(const L* p, size_t i);
+template <>
+__device__ __forceinline__ float logit_at<float>(const float* p, size_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float logit_at<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) {
+  return __bfloat162float(p[i]);
+}
+template <>
+__device__ __forceinline__ float logit_at<__half>(const __half* p, size_t i) { return __half2float(p[i]); }
+
+template <typename L>
+__global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* logits, int V, int B, int K1,
+                                                                      const int64_t* verify, int64_t* posterior,
+                                                                      int32_t* accept, int64_t* bonus,
+                                                                      unsigned long long* words,
+                                                                      unsigned int* done, unsigned int* status) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  __shared__ unsigned long long red[kVerifyThreads / 32];
+  __shared__ int last;
+  const int row = blockIdx.y;
+  const int v0 = blockIdx.x * kVerifyChunk;
+  const int v1 = min(V, v0 + kVerifyChunk);
+  const L* src = logits + (size_t)row * V;
+  unsigned long long best = 0ull;
+  for (int v = v0 + threadIdx.x; v < v1; v += kVerifyThreads) {
+    const float x = logit_at<L>(src, v);
+    if (!isnan(x)) {
+      const unsigned long long k = argmax_key(x, (uint32_t)v);
+      best = k > best ? k : best;
+    }
+  }
+  best = warp_max_u64(best);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long k = red[0];
+    for (int w = 1; w < kVerifyThreads / 32; ++w) k = red[w] > k ? red[w] : k;
+    if (k) atomicMax(words + row, k);
+    __threadfence();
+    const unsigned int total = gridDim.x * gridDim.y;
+    last = atomicAdd(done, 1u) == total - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int b = threadIdx.x; b < B; b += kVerifyThreads) {
+    int a = 0;
+    bool matching = true;
+    for (int j = 0; j < K1; ++j) {
+      const unsigned long long k = __ldcg(words + (size_t)b * K1 + j);
+      if (!k) atomicOr(status, 4u /* DD_STATUS_NO_ARGMAX */);
+      const int64_t tok = k ? (int64_t)argmax_key_index(k) : 0;
+      posterior[(size_t)b * K1 + j] = tok;
+      if (matching && j + 1 < K1 && verify[(size_t)b * K1 + j + 1] == tok) {
+        ++a;
+      } else {
+        matching = false;
+      }
+    }
+    accept[b] = a;
+    bonus[b] = posterior[(size_t)b * K1 + a];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < B * K1; i += kVerifyThreads) words[i] = 0ull;
+  if (threadIdx.x == 0) *done = 0u;
+}
+
 }  // namespace dd

@@ -288,6 +288,33 @@ class DraftCorrectionGraphRunner:
         return acc, bonus
 
     @torch.inference_mode()
+    def verify_accept(self, target_logits: torch.Tensor, verify_ids: torch.Tensor):
+        """Greedy verify fused with acceptance (code/dflash.py:472-485).
+
+        target_logits [B, K+1, V] (bf16, fp16 or fp32), verify_ids [B, K+1].
+        Returns ``(posterior [B, K+1] int64, accept [B] int32, bonus [B] int64)``
+        with ``posterior = argmax(target_logits, -1)`` computed in the same pass.
+        """
+        dt = {torch.bfloat16: _lib.DD_BF16, torch.float16: _lib.DD_FP16, torch.float32: _lib.DD_F32}
+        if target_logits.dtype not in dt:
+            raise TypeError(f"target_logits dtype {target_logits.dtype}")
+        logits = target_logits.to(self.device).contiguous()
+        v = verify_ids.to(self.device, torch.long).contiguous()
+        B, K1, V = logits.shape
+        if B != self.batch_size or V != self.vocab_size or tuple(v.shape) != (B, K1):
+            raise ValueError(f"expected logits [{self.batch_size}, K+1, {self.vocab_size}] and verify_ids [B, K+1]")
+        posterior = torch.empty(B, K1, dtype=torch.long, device=self.device)
+        acc = torch.empty(B, dtype=torch.int32, device=self.device)
+        bonus = torch.empty(B, dtype=torch.long, device=self.device)
+        _lib.check(
+            self._lib.dd_verify_accept(self._h, logits.data_ptr(), dt[logits.dtype], K1, v.data_ptr(),
+                                       posterior.data_ptr(), acc.data_ptr(), bonus.data_ptr(),
+                                       torch.cuda.current_stream(self.device).cuda_stream),
+            self._h, "dd_verify_accept",
+        )
+        return posterior, acc, bonus
+
+    @torch.inference_mode()
     def draft_block(self, last_token: torch.Tensor, parallel_hiddens: torch.Tensor,
                     base_logits_out: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         """Draft side of one block with the lm_head fused (code/dflash.py:424-439).

@@ -45,6 +45,7 @@ extern "C" {
 
 #define DD_BF16 0
 #define DD_FP16 1
+#define DD_F32 2   /* logits only (dd_verify_accept) */
 
 /* Device status bits (dd_get_status). */
 #define DD_STATUS_TIMEOUT 1u       /* a bounded wait inside a kernel gave up */
@@ -178,6 +179,18 @@ int dd_set_vocab_shard(dd_handle* h, int32_t rank, int32_t world, int64_t vocab_
  * when it runs out the step uses the words that arrived and the status word
  * gets DD_STATUS_TIMEOUT. */
 int dd_set_exchange_timeout(dd_handle* h, uint64_t timeout_ns);
+
+/* The target-side half of code/dflash.py:472-485 fused into one pass:
+ * posterior[b, j] = argmax_v target_logits[b, j, v] (lowest index on ties, as
+ * torch.argmax) and the greedy acceptance of verify_ids against it; the
+ * [B, k1, V] logits are read once and no intermediate is written.
+ *   target_logits [B, k1, V] (DD_BF16, DD_FP16 or DD_F32), V = cfg.vocab
+ *   verify_ids [B, k1] int64; posterior_out [B, k1] int64;
+ *   accept_out [B] int32 (accepted draft tokens); bonus_out [B] int64.
+ * k1 <= 64.  Calls on one handle must not overlap on the GPU. */
+int dd_verify_accept(dd_handle* h, const void* target_logits, int32_t logits_dtype, int32_t k1,
+                     const int64_t* verify_ids, int64_t* posterior_out, int32_t* accept_out,
+                     int64_t* bonus_out, void* stream);
 
 /* Launch kinds reported by dd_read_timing. */
 #define DD_PHASE_Z 1      /* z = parallel_hiddens @ W_z^T */

@@ -1,0 +1,65 @@
+"""Fused target verify + acceptance (dd_verify_accept) against torch.argmax
+and the oracle's acceptance (code/dflash.py:472-485): integers, so exact."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import draft_oracle as O
+from tests.gpu_helpers import random_modules
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _require_gpu():
+    if not torch.cuda.is_available() or torch.cuda.get_device_capability(0)[0] != 10:
+        pytest.fail("GPU tests need an sm_100 device")
+
+
+def _runner(B, V):
+    from domino_b200 import DraftCorrectionGraphRunner
+
+    draft, target = random_modules(64, 64, 96, V, seed=V % 97)
+    return DraftCorrectionGraphRunner(draft, target, B, 15, 64, 64, V, 1, torch.device("cuda", 0), use_graph=False)
+
+
+def _case(B, K1, V, dtype, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    logits = torch.randn(B, K1, V, generator=g, device="cuda").to(dtype)
+    if B > 1:
+        logits[1, 3] = 0.5                      # a constant row: every index ties, 0 wins
+        logits[1, 4, 17] = logits[1, 4, V - 5] = 50.0  # a duplicated maximum: the lower index wins
+    post = torch.argmax(logits.float(), dim=-1)
+    verify = torch.randint(0, V, (B, K1), generator=g, device="cuda")
+    for b in range(B):
+        a = (b * 5) % K1
+        verify[b, 1:a + 1] = post[b, :a]
+    return logits, verify, post
+
+
+@pytest.mark.parametrize("V", [5003, 20011])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_verify_accept_matches_argmax_and_acceptance(V, dtype):
+    B, K1 = 4, 16
+    r = _runner(B, V)
+    for seed in range(2):  # two calls in a row: the scratch clears itself
+        logits, verify, post_ref = _case(B, K1, V, dtype, seed)
+        post, acc, bonus = r.verify_accept(logits, verify)
+        assert r.status() == 0
+        assert torch.equal(post, post_ref)
+        ea, eb = O.accept(verify.cpu().numpy(), post_ref.cpu().numpy())
+        assert np.array_equal(acc.cpu().numpy(), ea)
+        assert np.array_equal(bonus.cpu().numpy(), eb)
+    r.close()
+
+
+def test_verify_accept_full_vocab_and_full_acceptance():
+    V, B, K1 = 151936, 2, 16
+    r = _runner(B, V)
+    logits, verify, post_ref = _case(B, K1, V, torch.bfloat16, 5)
+    verify[:, 1:] = post_ref[:, :-1]               # the target agrees everywhere
+    post, acc, bonus = r.verify_accept(logits, verify)
+    assert torch.equal(post, post_ref)
+    assert acc.tolist() == [K1 - 1] * B
+    assert torch.equal(bonus, post_ref[:, -1])
+    r.close()
