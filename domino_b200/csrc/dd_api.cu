@@ -93,6 +93,14 @@ struct dd_handle {
   unsigned int* xdone = nullptr;        // per-slot finished-CTA counters
   unsigned long long* peer[kMaxRanks] = {};
   unsigned long long xtimeout_ns = 2000ull * 1000 * 1000;
+  // Packed copies of the streamed weights (pack_tiles_kernel), made by
+  // dd_set_weights unless the layout is set to row-major.
+  bool pack = true;
+  void* pk_wz = nullptr;
+  void* pk_ws = nullptr;
+  void* pk_fc2 = nullptr;
+  void* pk_whh = nullptr;
+  void* pk_lm = nullptr;
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
@@ -349,10 +357,13 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
       p.base_out = base_out;
       p.kpos = positions;
       p.npre = npre;
+      p.packed[0] = static_cast<const uint8_t*>(h->pk_lm);
+      p.packed[1] = static_cast<const uint8_t*>(h->pk_wz);
       rc = launch_gemv<T, PH_ZLM>(h, h->tm_lm, &h->tm_wz, tm_x, p, PhaseClass::Big, true, st);
     } else {
       p.nseg = 1;
       p.seg[0] = {c.emb_dim, 0, EPI_ZPROJ};
+      p.packed[0] = static_cast<const uint8_t*>(h->pk_wz);
       rc = launch_gemv<T, PH_Z>(h, h->tm_wz, nullptr, tm_x, p, PhaseClass::Big, true, st);
     }
     if (rc) return rc;
@@ -396,6 +407,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     p.n_valid = c.batch;
     p.gh_out = h->ghbuf;
     p.b_hh = h->w.b_hh;
+    p.packed[0] = static_cast<const uint8_t*>(h->pk_whh);
     rc = launch_gemv<T, PH_GH>(h, h->tm_whh, nullptr, h->tm_h[cur], p, PhaseClass::Small, true, st);
     if (rc) return rc;
     CellParams cp;
@@ -439,6 +451,8 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.mid_out = h->midbuf;
       p.gh_out = h->ghbuf;
       p.b_hh = h->w.b_hh;
+      p.packed[0] = static_cast<const uint8_t*>(h->pk_ws);
+      p.packed[1] = static_cast<const uint8_t*>(h->pk_whh);
       rc = launch_gemv<T, PH_SGH>(h, h->tm_ws, last ? nullptr : &h->tm_whh, h->tm_h[cur], p, PhaseClass::Small, true, st);
       if (rc) return rc;
     }
@@ -456,6 +470,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.base_voff = base_voff;
       p.xslot0 = npre + t;
       p.xslot1 = npre + t + 1;
+      p.packed[0] = static_cast<const uint8_t*>(h->pk_fc2);
       p.base_rows_per_b = positions;
       p.base_pos_off = npre;
       p.fc2_bias = h->w.fc2_bias;
@@ -496,6 +511,25 @@ int check_ready(dd_handle* h) {
   if (!h->have_weights) return fail(h, DD_EINVAL, "dd_set_weights has not been called");
   if (!h->w.table) return fail(h, DD_EINVAL, "weights.table is null (build it with dd_build_table)");
   return use_device(h);
+}
+
+void free_packed(dd_handle* h) {
+  void** bufs[] = {&h->pk_wz, &h->pk_ws, &h->pk_fc2, &h->pk_whh, &h->pk_lm};
+  for (void** b : bufs) {
+    if (*b) cudaFree(*b);
+    *b = nullptr;
+  }
+}
+
+// Packed copy of W [rows x K] (row stride ld) for 1-D bulk streaming.
+int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long long ld, void** out) {
+  const int KC = ceil_div(K, kChunkK);
+  const long long blocks = (long long)ceil_div(rows, kTileM) * KC;
+  DD_CUDA(h, cudaMalloc(out, (size_t)blocks * kATileBytes));
+  pack_tiles_kernel<<<(unsigned)blocks, 256>>>(static_cast<const uint16_t*>(w), rows, K, ld, KC,
+                                               static_cast<uint4*>(*out));
+  DD_CUDA(h, cudaGetLastError());
+  return DD_OK;
 }
 
 }  // namespace
@@ -547,6 +581,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", h->ctas_per_sm_big, 1, 2);
   h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", h->ctas_per_sm_small, 1, 2);
   h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
+  h->pack = env_int("DD_PACK_WEIGHTS", 1, 0, 1) != 0;
   int prev = 0;
   cudaGetDevice(&prev);
   auto cleanup_fail = [&](int code) {
@@ -612,8 +647,32 @@ int dd_set_weights(dd_handle* h, const dd_weights* w) {
   if (!rc && w->lm_head)
     rc = encode_kmajor(h, &h->tm_lm, w->lm_head, c.dtype, c.hidden, h->v_local, w->lm_head_ld, kTileM);
   if (rc) return rc;
+  free_packed(h);
+  if (h->pack) {
+    // The weights may still be being written on another stream of this
+    // process: wait for the device, pack, and wait for the packing.
+    DD_CUDA(h, cudaDeviceSynchronize());
+    const long long G = c.gru_hidden;
+    rc = pack_matrix(h, w->fc1, c.emb_dim, c.hidden, w->fc1_ld, &h->pk_wz);
+    if (!rc) rc = pack_matrix(h, esz + (size_t)c.hidden * 2, c.emb_dim, G, w->fc1_ld, &h->pk_ws);
+    if (!rc) rc = pack_matrix(h, w->fc2, h->v_local, c.emb_dim, w->fc2_ld, &h->pk_fc2);
+    if (!rc) rc = pack_matrix(h, w->w_hh, 3 * G, G, w->w_hh_ld, &h->pk_whh);
+    if (!rc && w->lm_head) rc = pack_matrix(h, w->lm_head, h->v_local, c.hidden, w->lm_head_ld, &h->pk_lm);
+    if (!rc) DD_CUDA(h, cudaDeviceSynchronize());
+    if (rc) {
+      free_packed(h);
+      return rc;
+    }
+  }
   h->w = *w;
   h->have_weights = true;
+  return DD_OK;
+}
+
+int dd_set_weight_layout(dd_handle* h, int packed) {
+  if (!h) return DD_EINVAL;
+  h->pack = packed != 0;
+  h->have_weights = false;  // dd_set_weights must run again
   return DD_OK;
 }
 
@@ -867,6 +926,7 @@ int dd_destroy(dd_handle* h) {
                   h->counters, h->status,  h->xbuf,    h->xseq,    h->xdone, h->vwords, h->vdone};
   for (void* p : ptrs)
     if (p) cudaFree(p);
+  free_packed(h);
   for (cudaEvent_t e : h->ev)
     if (e) cudaEventDestroy(e);
   cudaSetDevice(prev);
@@ -958,6 +1018,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.err[0] = 0;
   h.N1 = round_up(c.batch, 16);
   h.N2 = round_up(2 * c.batch, 16);
+  h.pack = false;  // packing would allocate: stream the caller's row-major weights
   h.v_off = 0;
   h.v_local = c.vocab;  // unsharded
   h.world = 1;

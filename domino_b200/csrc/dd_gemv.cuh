@@ -92,6 +92,10 @@ struct GemvSeg {
 
 struct GemvParams {
   GemvSeg seg[2];
+  // Packed weights (see pack_tiles_kernel): segment s's (tile, k-chunk) block
+  // is the 16 KB at packed[s] + (tile * KC + kc) * 16384, already in the
+  // swizzled order the MMA reads; null = load the row-major matrix by TMA.
+  const uint8_t* packed[2];
   int nseg;
   int K, KC;
   int N;             // MMA N: X rows per pass, multiple of 16, <= 256
@@ -397,6 +401,39 @@ __device__ __forceinline__ void publish_words(const GemvParams& p, int ept, vola
   }
 }
 
+// One-time relayout of a row-major weight matrix W [rows x K] (row stride ld
+// elements, 2-byte elements) into 16 KB blocks, one per (128-row tile, 64-wide
+// k-chunk), tile-major: block (t, kc) holds rows t*128 .. t*128+127, columns
+// kc*64 .. kc*64+63, laid out exactly as a 128B-swizzled TMA box lands in
+// shared memory (16-byte chunk j of row r at chunk j ^ (r & 7)); rows and
+// columns past the matrix are zero.  A phase then streams each CTA's units as
+// one contiguous run of 16 KB bulk copies.
+__global__ void __launch_bounds__(256) pack_tiles_kernel(const uint16_t* __restrict__ w, long long rows, long long K,
+                                                         long long ld, int KC, uint4* __restrict__ out) {
+  const long long blk = blockIdx.x;  // = tile * KC + kc
+  const long long tile = blk / KC;
+  const int kc = (int)(blk - tile * KC);
+  uint4* dst = out + blk * (kATileBytes / 16);
+  for (int i = threadIdx.x; i < kTileM * 8; i += blockDim.x) {
+    const int r = i >> 3, j = i & 7;
+    const long long row = tile * kTileM + r;
+    const long long col = (long long)kc * kChunkK + j * 8;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (row < rows) {
+      const uint16_t* src = w + row * ld + col;
+      if (col + 8 <= K && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        v = *reinterpret_cast<const uint4*>(src);
+      } else {
+        uint16_t e[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) e[q] = (col + q < K) ? src[q] : (uint16_t)0;
+        memcpy(&v, e, 16);
+      }
+    }
+    dst[r * 8 + (j ^ (r & 7))] = v;
+  }
+}
+
 template <typename T, int kPhase>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
@@ -474,9 +511,15 @@ __global__ void __launch_bounds__(kThreads, 2)
         const long long tile = u / KC;
         const int kc = (int)(u % KC);
         const bool s1 = tile >= p.seg[0].tiles;
-        const int row0 = (int)((s1 ? tile - p.seg[0].tiles : tile) * kTileM);
-        tma_load_2d(ring + (size_t)stage * p.stage_bytes, s1 ? &tmA1 : &tmA0, &full[stage], kc * kChunkK, row0,
-                    pol_w);
+        const long long seg_tile = s1 ? tile - p.seg[0].tiles : tile;
+        const uint8_t* pk = p.packed[s1 ? 1 : 0];
+        if (pk) {
+          bulk_load(ring + (size_t)stage * p.stage_bytes, pk + (size_t)(seg_tile * KC + kc) * kATileBytes,
+                    kATileBytes, &full[stage], pol_w);
+        } else {
+          tma_load_2d(ring + (size_t)stage * p.stage_bytes, s1 ? &tmA1 : &tmA0, &full[stage], kc * kChunkK,
+                      (int)(seg_tile * kTileM), pol_w);
+        }
       };
       auto load_b = [&](int stage, long long u) {
         const int kc = (int)(u % KC);

@@ -73,6 +73,9 @@ class DraftCorrectionGraphRunner:
                    GPU); every rank must construct the runner with the same
                    weights and call it with the same inputs.  The per-step
                    argmax is combined across GPUs inside the kernels.
+      pack_weights: keep a tile-packed copy of the streamed matrices (W_z,
+                   W_s, W_hh, fc2, lm_head) that streams ~6 % faster; False
+                   streams the module parameters in place (no extra memory).
     """
 
     def __init__(
@@ -88,6 +91,7 @@ class DraftCorrectionGraphRunner:
         device: torch.device,
         use_graph: bool = True,
         vocab_shard: bool = False,
+        pack_weights: bool = True,
     ):
         self.steps = int(steps)
         self.draft_model = draft_model
@@ -192,6 +196,7 @@ class DraftCorrectionGraphRunner:
                 table=self._table.data_ptr(), table_ld=self._table.stride(0),
                 lm_head=_ptr(lm_rows), lm_head_ld=lm_rows.stride(0) if lm_rows is not None else 0,
             )
+            _lib.check(self._lib.dd_set_weight_layout(self._h, 1 if pack_weights else 0), self._h, "layout")
             _lib.check(self._lib.dd_set_weights(self._h, ctypes.byref(self._weights)), self._h, "dd_set_weights")
 
             B, S = self.batch_size, self.steps

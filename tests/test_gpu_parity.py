@@ -121,6 +121,25 @@ def test_graph_replay_matches_eager_and_is_deterministic():
         assert torch.equal(a, b) and torch.equal(a, c)
 
 
+@pytest.mark.parametrize("B,P", [(1, 1), (5, 3)])
+def test_packed_and_row_major_weights_agree_exactly(B, P):
+    """The packed tile layout feeds the tensor cores the same bytes as TMA."""
+    H, G, E, V, S = 192, 128, 328, 3001, 13
+    draft, target = random_modules(H, G, E, V, seed=61 + B, fc2_std=0.08, fc1_bias=True)
+    rp = make_runner(draft, target, B, S, H, G, V, P, use_graph=False, pack_weights=True)
+    rr = make_runner(draft, target, B, S, H, G, V, P, use_graph=False, pack_weights=False)
+    prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=2)
+    assert torch.equal(rp(prefix, ph, base), rr(prefix, ph, base))
+    K = P - 1 + S
+    g = torch.Generator().manual_seed(4)
+    ph2 = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    last = torch.randint(0, V, (B,), generator=g).cuda()
+    vp, bp = rp.draft_block(last, ph2)
+    vr, br = rr.draft_block(last, ph2)
+    assert torch.equal(vp, vr) and torch.equal(bp, br)
+    assert rp.status() == 0 and rr.status() == 0
+
+
 def test_draft_block_fused_lm_head():
     B, H, G, E, V, S, P = 3, 128, 128, 192, 1500, 13, 3
     draft, target = random_modules(H, G, E, V, seed=31, fc2_std=0.08)
