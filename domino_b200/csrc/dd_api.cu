@@ -72,14 +72,20 @@ struct dd_handle {
   // environment at dd_create: DD_RING_KB_BIG, DD_RING_KB_SMALL,
   // DD_MIN_SMEM_KB_BIG, DD_CTAS_PER_SM_BIG, DD_CTAS_PER_SM_SMALL).  "Big" phases stream the large
   // matrices (fc2, lm_head + W_z, the table); "small" ones W_s / W_hh.
-  // Defaults measured on B200 (cfg: H = G = 4096, E = 12288, V = 151936):
-  // two CTAs per SM with ~100 KB rings stream fc2 at ~6.9 TB/s, against
-  // ~5.5 TB/s for one CTA per SM at any ring depth up to 216 KB.
-  int ring_kb_big = 100;
-  int ring_kb_small = 100;
+  // Defaults measured on B200 (H = G = 4096, E = 12288, V = 151936): two
+  // CTAs per SM with 72 KB rings (4 stages at batch <= 8) stream fc2 at
+  // ~7.1 TB/s, and leave room on each SM for one CTA of the next phase, which
+  // prefetches its weights under programmatic dependent launch; 100 KB rings
+  // (no room) give ~6.5-6.9 TB/s and one CTA per SM ~5.5 TB/s at any depth.
+  // More accumulators per slot and the packed weight layout measured no gain
+  // at this shape, so both default off.
+  int ring_kb_big = 72;
+  int ring_kb_small = 72;
   int min_smem_kb_big = 0;
   int ctas_per_sm_big = 2;
   int ctas_per_sm_small = 2;
+  int max_nacc = 1;               // DD_NACC
+  int tmem_cols_per_cta = 128;    // DD_TMEM_COLS
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
   // Vocab sharding (dd_set_vocab_shard): this rank owns vocab rows
   // [v_off, v_off + v_local) of fc2 / lm_head; world == 1 means unsharded.
@@ -95,7 +101,7 @@ struct dd_handle {
   unsigned long long xtimeout_ns = 2000ull * 1000 * 1000;
   // Packed copies of the streamed weights (pack_tiles_kernel), made by
   // dd_set_weights unless the layout is set to row-major.
-  bool pack = true;
+  bool pack = false;
   void* pk_wz = nullptr;
   void* pk_ws = nullptr;
   void* pk_fc2 = nullptr;
@@ -237,10 +243,15 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   p.stage_bytes = kATileBytes + p.b_bytes;
   const uint32_t ring_budget =
       p.N > 64 ? 196u * 1024u : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
-  p.stages = std::max(2, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  p.stages = std::max(4, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  if ((size_t)p.stages * p.stage_bytes + 1024 + kSmemTail > 227 * 1024) p.stages = (227 * 1024 - 1024 - kSmemTail) / p.stage_bytes;
   p.acc_slots = p.N <= 128 ? 2 : 1;
+  // Up to four accumulators per slot within the per-CTA TMEM budget, so that
+  // co-resident CTAs (2 per SM plus the next phase's) never wait for TMEM.
+  p.nacc = 1;
+  while (p.nacc < h->max_nacc && p.acc_slots * p.nacc * 2 * p.N <= h->tmem_cols_per_cta) p.nacc *= 2;
   uint32_t cols = 32;
-  while (cols < (uint32_t)(p.acc_slots * p.N)) cols <<= 1;
+  while (cols < (uint32_t)(p.acc_slots * p.nacc * p.N)) cols <<= 1;
   p.tmem_cols = cols;
   p.idesc = idesc_f16((uint32_t)p.N, std::is_same<T, __half>::value ? 0u : 1u);
   p.partials = h->partials;
@@ -581,7 +592,9 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", h->ctas_per_sm_big, 1, 2);
   h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", h->ctas_per_sm_small, 1, 2);
   h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
-  h->pack = env_int("DD_PACK_WEIGHTS", 1, 0, 1) != 0;
+  h->pack = env_int("DD_PACK_WEIGHTS", 0, 0, 1) != 0;
+  h->max_nacc = env_int("DD_NACC", h->max_nacc, 1, 4);
+  h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", h->tmem_cols_per_cta, 32, 512);
   int prev = 0;
   cudaGetDevice(&prev);
   auto cleanup_fail = [&](int code) {

@@ -106,6 +106,7 @@ struct GemvParams {
   uint32_t stage_bytes;
   uint32_t b_bytes;
   int acc_slots;
+  int nacc;          // independent accumulators per slot; K-step i goes to accumulator i % nacc
   uint32_t tmem_cols;
   uint32_t idesc;
   int B, t, V, E, G3;
@@ -194,6 +195,7 @@ __device__ __forceinline__ bool wait_ns(uint64_t* bar, uint32_t parity, uint64_t
 // Context an epilogue thread needs to read its (possibly split) accumulator.
 struct AccView {
   uint32_t taddr;      // TMEM address of this thread's lane, column 0 of the slot
+  int nacc;            // accumulators of the slot, N columns apart
   bool combine;        // split tile finished here: sum partials of all segments
   int nseg, myseg, c_lo;
   long long T;
@@ -204,12 +206,25 @@ struct AccView {
   int G, KC;
 };
 
+// This CTA's part of 16 accumulator columns [ch*16, ch*16+16): the sum of the
+// slot's accumulators in a fixed order.
+__device__ __forceinline__ void acc_local(const AccView& a, int ch, float* t) {
+  tmem_ld16(a.taddr + ch * 16, *reinterpret_cast<float(*)[16]>(t));
+  tmem_ld_wait();
+  for (int i = 1; i < a.nacc; ++i) {
+    float u[16];
+    tmem_ld16(a.taddr + i * a.N + ch * 16, u);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) t[j] += u[j];
+  }
+}
+
 // 16 accumulator columns [ch*16, ch*16+16) of this thread's row, summed over
 // the tile's segments in CTA order when the tile was split.
 __device__ __forceinline__ void acc_chunk(const AccView& a, int ch, float* v) {
   float t[16];
-  tmem_ld16(a.taddr + ch * 16, t);
-  tmem_ld_wait();
+  acc_local(a, ch, t);
   if (!a.combine) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) v[j] = t[j];
@@ -562,7 +577,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         const uint32_t use = (uint32_t)(acc_it / p.acc_slots);
         if (!mbar_wait_bounded(&acce[slot], (use & 1u) ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + (uint32_t)(slot * p.N);
+        const uint32_t d = tmem_base + (uint32_t)(slot * p.N * p.nacc);
         for (int kc = kc0; kc < kc1; ++kc, ++it) {
           const int stage = (int)(it % p.stages);
           const uint32_t round = (uint32_t)(it / p.stages);
@@ -574,9 +589,14 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint32_t a_addr = smem_u32(ring + (size_t)stage * p.stage_bytes);
           const uint64_t adesc = smem_desc_k_sw128(a_addr);
           const uint64_t bdesc = smem_desc_k_sw128(a_addr + kATileBytes);
+          // Consecutive K-steps go to different accumulators so that the
+          // tensor pipe overlaps them instead of chaining on one accumulator.
 #pragma unroll
-          for (int k = 0; k < kChunkK / 16; ++k)
-            mma_f16_ss(d, adesc + 2 * k, bdesc + 2 * k, p.idesc, (kc > kc0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kChunkK / 16; ++k) {
+            const int ks = (kc - kc0) * (kChunkK / 16) + k;
+            const int acc = ks % p.nacc;
+            mma_f16_ss(d + (uint32_t)(acc * p.N), adesc + 2 * k, bdesc + 2 * k, p.idesc, ks >= p.nacc ? 1u : 0u);
+          }
           mma_commit(&empty[stage]);
         }
         if (!ok) break;
@@ -612,7 +632,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       const bool valid = row < sg.rows;
 
       AccView a;
-      a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N);
+      a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N * p.nacc);
+      a.nacc = p.nacc;
       a.combine = false;
       a.nseg = 1;
       a.myseg = 0;
@@ -636,8 +657,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         float* mine = p.partials + (size_t)partial_slot(c, tile, U, G, KC) * p.N * kTileM;
         for (int ch = 0; ch < p.N / 16; ++ch) {
           float v[16];
-          tmem_ld16(a.taddr + ch * 16, v);
-          tmem_ld_wait();
+          acc_local(a, ch, v);
 #pragma unroll
           for (int j = 0; j < 16; ++j) __stcg(mine + (size_t)(ch * 16 + j) * kTileM + r, v[j]);
         }

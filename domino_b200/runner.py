@@ -74,8 +74,8 @@ class DraftCorrectionGraphRunner:
                    weights and call it with the same inputs.  The per-step
                    argmax is combined across GPUs inside the kernels.
       pack_weights: keep a tile-packed copy of the streamed matrices (W_z,
-                   W_s, W_hh, fc2, lm_head) that streams ~6 % faster; False
-                   streams the module parameters in place (no extra memory).
+                   W_s, W_hh, fc2, lm_head), streamed with 1-D bulk copies;
+                   the default streams the module parameters in place.
     """
 
     def __init__(
@@ -91,7 +91,7 @@ class DraftCorrectionGraphRunner:
         device: torch.device,
         use_graph: bool = True,
         vocab_shard: bool = False,
-        pack_weights: bool = True,
+        pack_weights: bool = False,
     ):
         self.steps = int(steps)
         self.draft_model = draft_model

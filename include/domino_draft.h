@@ -84,16 +84,17 @@ typedef struct dd_weights {
 int dd_create(const dd_config* cfg, int device, dd_handle** out);
 
 /* Point the handle at the head's weights and prepare their TMA descriptors.
- * With the packed layout (the default) it also copies W_z, W_s, W_hh, fc2 and
- * lm_head once into handle-owned buffers of 16 KB tiles in the order the
- * tensor cores read them, which stream ~6 % faster than the row-major
- * originals (one extra copy of those matrices in HBM; it synchronises the
- * device).  Call again after the weights change. */
+ * With the packed layout (dd_set_weight_layout) it also copies W_z, W_s,
+ * W_hh, fc2 and lm_head once into handle-owned buffers of 16 KB tiles in the
+ * order the tensor cores read them (one extra copy of those matrices in HBM;
+ * it synchronises the device).  Call again after the weights change. */
 int dd_set_weights(dd_handle* h, const dd_weights* w);
 
-/* packed = 1 (default; DD_PACK_WEIGHTS=0 in the environment turns it off at
- * dd_create) or 0 to stream the caller's row-major weights in place with no
- * extra memory.  Takes effect at the next dd_set_weights. */
+/* packed = 0 (default: stream the caller's row-major weights in place, no
+ * extra memory) or 1 (stream the packed copy with 1-D bulk copies; measured
+ * equal speed at the default launch shape; DD_PACK_WEIGHTS=1 in the
+ * environment selects it at dd_create).  Takes effect at the next
+ * dd_set_weights. */
 int dd_set_weight_layout(dd_handle* h, int packed);
 
 /* table[v, :] = embed[v, :] @ W_ih^T + b_ih, rounded to the weight dtype
