@@ -522,9 +522,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint64_t pol_x = policy_evict_last();
       const long long n_my = u_end - u_begin;
       const int pre = (int)(n_my < p.stages ? n_my : p.stages);
-      auto load_a = [&](int stage, long long u) {
-        const long long tile = u / KC;
-        const int kc = (int)(u % KC);
+      // Unit u of this CTA's range is (tile, kc) = (u / KC, u % KC); the
+      // loops below advance (tile, kc) and the ring position incrementally.
+      auto load_a = [&](int stage, long long tile, int kc) {
         const bool s1 = tile >= p.seg[0].tiles;
         const long long seg_tile = s1 ? tile - p.seg[0].tiles : tile;
         const uint8_t* pk = p.packed[s1 ? 1 : 0];
@@ -536,27 +536,45 @@ __global__ void __launch_bounds__(kThreads, 2)
                       (int)(seg_tile * kTileM), pol_w);
         }
       };
-      auto load_b = [&](int stage, long long u) {
-        const int kc = (int)(u % KC);
+      auto load_b = [&](int stage, int kc) {
         tma_load_2d(ring + (size_t)stage * p.stage_bytes + kATileBytes, &tmB, &full[stage], kc * kChunkK, p.n_off,
                     pol_x);
       };
+      const long long tile_begin = u_begin / KC;
+      const int kc_begin = (int)(u_begin - tile_begin * KC);
+      long long tile = tile_begin;
+      int kc = kc_begin;
       // Weights first: they do not depend on the previous kernel.
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], kATileBytes + p.b_bytes);
-        load_a(i, u_begin + i);
+        load_a(i, tile, kc);
+        if (++kc == KC) {
+          kc = 0;
+          ++tile;
+        }
       }
       pdl_wait_primary();
       fence_proxy_async_global();
-      for (int i = 0; i < pre; ++i) load_b(i, u_begin + i);
+      for (int i = 0, kb = kc_begin; i < pre; ++i) {
+        load_b(i, kb);
+        if (++kb == KC) kb = 0;
+      }
+      int stage = pre == p.stages ? 0 : pre;
+      uint32_t parity = pre == p.stages ? 1u : 0u;
       long long it = pre;
       for (; it < n_my; ++it) {
-        const int stage = (int)(it % p.stages);
-        const uint32_t round = (uint32_t)(it / p.stages);
-        if (!mbar_wait_bounded(&empty[stage], (round & 1u) ^ 1u, abort_flag)) break;
+        if (!mbar_wait_bounded(&empty[stage], parity ^ 1u, abort_flag)) break;
         mbar_arrive_expect_tx(&full[stage], kATileBytes + p.b_bytes);
-        load_a(stage, u_begin + it);
-        load_b(stage, u_begin + it);
+        load_a(stage, tile, kc);
+        load_b(stage, kc);
+        if (++kc == KC) {
+          kc = 0;
+          ++tile;
+        }
+        if (++stage == p.stages) {
+          stage = 0;
+          parity ^= 1u;
+        }
       }
       *issued = it;
     }
@@ -566,6 +584,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       // ------------------------------------------------ MMA issuer
       long long u = u_begin;
       long long it = 0;
+      int stage = 0;
+      uint32_t parity = 0;
       int acc_it = 0;
       bool ok = true;
       while (ok && u < u_end) {
@@ -579,9 +599,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         tc_fence_after();
         const uint32_t d = tmem_base + (uint32_t)(slot * p.N * p.nacc);
         for (int kc = kc0; kc < kc1; ++kc, ++it) {
-          const int stage = (int)(it % p.stages);
-          const uint32_t round = (uint32_t)(it / p.stages);
-          if (!mbar_wait_bounded(&full[stage], round & 1u, abort_flag)) {
+          if (!mbar_wait_bounded(&full[stage], parity, abort_flag)) {
             ok = false;
             break;
           }
@@ -598,6 +616,10 @@ __global__ void __launch_bounds__(kThreads, 2)
             mma_f16_ss(d + (uint32_t)(acc * p.N), adesc + 2 * k, bdesc + 2 * k, p.idesc, ks >= p.nacc ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
+          if (++stage == p.stages) {
+            stage = 0;
+            parity ^= 1u;
+          }
         }
         if (!ok) break;
         mma_commit(&accf[slot]);
