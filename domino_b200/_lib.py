@@ -32,7 +32,7 @@ EXPORTS = (
     "dd_get_exchange_buffer", "dd_ipc_export", "dd_ipc_open", "dd_ipc_close", "dd_set_vocab_shard",
     "dd_set_exchange_timeout", "dd_verify_accept", "dd_set_weight_layout",
 )
-PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell"}
+PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell", 8: "gather"}
 
 
 class DDConfig(ctypes.Structure):

@@ -93,8 +93,15 @@ struct dd_handle {
   int v_local = 0;
   int world = 1;
   int rank = 0;
-  unsigned long long* xbuf = nullptr;   // this rank's exchange buffer
+  unsigned long long* xbuf = nullptr;   // this rank's exchange buffer (also holds mid and gh)
   size_t xbuf_bytes = 0;
+  size_t xsflag_off = 0, xmid_off = 0, xgh_off = 0;  // offsets inside xbuf (u64 units / bytes)
+  unsigned int* xsdone = nullptr;       // per-slot finished-CTA counters of the s / gh phase
+  // Sharded s / gh phase: rank j computes rows [e0[j], e1[j]) of W_s and
+  // [g0[j], g1[j]) of W_hh (128-row aligned); off when a matrix has fewer
+  // 128-row tiles than ranks.
+  bool sgh_sharded = false;
+  int e0[kMaxRanks] = {}, e1[kMaxRanks] = {}, g0[kMaxRanks] = {}, g1[kMaxRanks] = {};
   unsigned long long* xseq = nullptr;   // call sequence number (device)
   unsigned int* xdone = nullptr;        // per-slot finished-CTA counters
   unsigned long long* peer[kMaxRanks] = {};
@@ -303,6 +310,10 @@ Exchange make_exchange(const dd_handle* h) {
   x.nslots = h->nslots;
   x.B = h->cfg.batch;
   x.timeout_ns = h->xtimeout_ns;
+  x.sflag_off = h->xsflag_off;
+  x.mid_off = h->xmid_off;
+  x.gh_off = h->xgh_off;
+  x.sdone = h->xsdone;
   return x;
 }
 
@@ -320,6 +331,7 @@ GemvParams base_params(const dd_handle* h) {
   p.base_out_ld = h->v_local;
   p.base_voff = h->v_off;
   p.xchg = make_exchange(h);
+  p.sflag_slot = -1;
   return p;
 }
 
@@ -334,9 +346,41 @@ __global__ void bump_sequence_kernel(unsigned long long* seq) {
 int begin_exchange(dd_handle* h, cudaStream_t st) {
   if (h->world <= 1) return DD_OK;
   DD_CUDA(h, cudaMemsetAsync(h->xdone, 0, (size_t)h->nslots * 4, st));
+  DD_CUDA(h, cudaMemsetAsync(h->xsdone, 0, (size_t)h->nslots * 4, st));
   Launch L(dim3(1), dim3(1), 0, st);
   DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, bump_sequence_kernel, h->xseq));
   return DD_OK;
+}
+
+// Sharded s / gh phase: copy the other ranks' mid / gh slices of `slot` here.
+int launch_gather(dd_handle* h, int slot, bool with_gh, cudaStream_t st) {
+  GatherParams gp;
+  memset(&gp, 0, sizeof(gp));
+  gp.xchg = make_exchange(h);
+  gp.xbuf = h->xbuf;
+  gp.slot = slot;
+  gp.mid_rows = 2 * h->cfg.batch;
+  gp.E = h->cfg.emb_dim;
+  gp.G3 = 3 * h->cfg.gru_hidden;
+  gp.B = h->cfg.batch;
+  long long vecs = 0;
+  for (int j = 0; j < h->world; ++j) {
+    gp.e0[j] = h->e0[j];
+    gp.e1[j] = h->e1[j];
+    gp.g0[j] = h->g0[j];
+    gp.g1[j] = h->g1[j];
+    if (j != h->rank)
+      vecs += (long long)gp.mid_rows * (h->e1[j] - h->e0[j]) / 8 +
+              (with_gh ? (long long)gp.B * (h->g1[j] - h->g0[j]) / 8 : 0);
+  }
+  gp.with_gh = with_gh ? 1 : 0;
+  gp.status = h->status;
+  const int grid = (int)std::max<long long>(1, std::min<long long>(2LL * h->num_sms, (vecs + 255) / 256));
+  int rc = timing_begin(h, DD_PHASE_GATHER, st);
+  if (rc) return rc;
+  Launch L(dim3(grid), dim3(256), 0, st);
+  DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, gather_slices_kernel, gp));
+  return timing_end(h, st);
 }
 
 // Z (+ lm_head) phase over the X = parallel_hiddens rows, in passes of <= 256 rows.
@@ -450,8 +494,14 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     {
       GemvParams p = base_params(h);
       p.nseg = last ? 1 : 2;
-      p.seg[0] = {c.emb_dim, 0, EPI_SPROJ_MID};
-      p.seg[1] = {3 * c.gru_hidden, 0, EPI_GH};
+      p.seg[0] = {c.emb_dim, 0, EPI_SPROJ_MID, 0};
+      p.seg[1] = {3 * c.gru_hidden, 0, EPI_GH, 0};
+      if (h->sgh_sharded) {
+        const int r = h->rank;
+        p.seg[0] = {h->e1[r] - h->e0[r], 0, EPI_SPROJ_MID, h->e0[r]};
+        p.seg[1] = {h->g1[r] - h->g0[r], 0, EPI_GH, h->g0[r]};
+        p.sflag_slot = npre + t;
+      }
       p.K = c.gru_hidden;
       p.N = h->N1;
       p.n_valid = c.batch;
@@ -466,6 +516,10 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.packed[1] = static_cast<const uint8_t*>(h->pk_whh);
       rc = launch_gemv<T, PH_SGH>(h, h->tm_ws, last ? nullptr : &h->tm_whh, h->tm_h[cur], p, PhaseClass::Small, true, st);
       if (rc) return rc;
+      if (h->sgh_sharded) {
+        rc = launch_gather(h, npre + t, !last, st);
+        if (rc) return rc;
+      }
     }
     {
       GemvParams p = base_params(h);
@@ -578,7 +632,19 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->v_local = c.vocab;
   const int npre_max = c.prefix_tokens - 1;
   h->nslots = npre_max + c.steps;
-  h->xbuf_bytes = ((size_t)2 * h->nslots * kMaxRanks * c.batch + (size_t)2 * h->nslots * kMaxRanks) * 8;
+  {
+    // exchange buffer: argmax words, their flags, s / gh flags, then mid and gh
+    const size_t words = (size_t)2 * h->nslots * kMaxRanks * c.batch;
+    const size_t flags = (size_t)2 * h->nslots * kMaxRanks;
+    h->xsflag_off = words + flags;  // u64 index
+    size_t bytes = (words + 2 * flags) * 8;
+    bytes = (bytes + 255) & ~size_t(255);
+    h->xmid_off = bytes;
+    bytes += ((size_t)h->N2 * c.emb_dim * 2 + 255) & ~size_t(255);
+    h->xgh_off = bytes;
+    bytes += ((size_t)c.batch * 3 * c.gru_hidden * 2 + 255) & ~size_t(255);
+    h->xbuf_bytes = bytes;
+  }
   h->max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
   auto env_int = [](const char* name, int def, int lo, int hi) {
     const char* v = getenv(name);
@@ -610,15 +676,14 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
     size_t bytes;
   } allocs[] = {
       {&h->zbuf, (size_t)c.batch * positions * c.emb_dim * es},
-      {&h->midbuf, (size_t)h->N2 * c.emb_dim * es},
       {&h->hbuf[0], (size_t)h->N1 * c.gru_hidden * es},
       {&h->hbuf[1], (size_t)h->N1 * c.gru_hidden * es},
-      {&h->ghbuf, (size_t)c.batch * 3 * c.gru_hidden * es},
       {(void**)&h->slots, (size_t)c.batch * h->nslots * 8},
       {(void**)&h->partials, (size_t)2 * h->max_ctas * 256 * kTileM * 4},
       {(void**)&h->counters, (size_t)h->max_tiles * 4},
       {(void**)&h->status, 64},
-      {(void**)&h->xbuf, ((size_t)2 * h->nslots * kMaxRanks * c.batch + (size_t)2 * h->nslots * kMaxRanks) * 8},
+      {(void**)&h->xbuf, h->xbuf_bytes},
+      {(void**)&h->xsdone, (size_t)h->nslots * 4},
       {(void**)&h->xseq, 64},
       {(void**)&h->xdone, (size_t)h->nslots * 4},
       {(void**)&h->vwords, (size_t)c.batch * dd_handle::kMaxVerifyPositions * 8},
@@ -630,6 +695,8 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
     if (cudaMemset(*a.p, 0, a.bytes) != cudaSuccess)
       return cleanup_fail(fail(nullptr, DD_ECUDA, "cudaMemset failed"));
   }
+  h->midbuf = reinterpret_cast<uint8_t*>(h->xbuf) + h->xmid_off;
+  h->ghbuf = reinterpret_cast<uint8_t*>(h->xbuf) + h->xgh_off;
   int rc = encode_kmajor(h, &h->tm_mid, h->midbuf, c.dtype, c.emb_dim, h->N2, c.emb_dim, h->N2);
   if (!rc) rc = encode_kmajor(h, &h->tm_h[0], h->hbuf[0], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
   if (!rc) rc = encode_kmajor(h, &h->tm_h[1], h->hbuf[1], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
@@ -881,6 +948,19 @@ int dd_set_vocab_shard(dd_handle* h, int32_t rank, int32_t world, int64_t vocab_
   h->rank = rank;
   h->v_off = (int)vocab_begin;
   h->v_local = (int)(vocab_end - vocab_begin);
+  // s / gh slices: contiguous near-equal runs of 128-row tiles
+  const int te = ceil_div(h->cfg.emb_dim, kTileM), tg = ceil_div(3LL * h->cfg.gru_hidden, kTileM);
+  h->sgh_sharded = world > 1 && te >= world && tg >= world;
+  for (int j = 0; j < world; ++j) {
+    auto split = [&](int tiles, int rows, int* lo, int* hi) {
+      const int base = tiles / world, extra = tiles % world;
+      const int t0 = j * base + std::min(j, extra), t1 = t0 + base + (j < extra ? 1 : 0);
+      *lo = std::min(rows, t0 * kTileM);
+      *hi = std::min(rows, t1 * kTileM);
+    };
+    split(te, h->cfg.emb_dim, &h->e0[j], &h->e1[j]);
+    split(tg, 3 * h->cfg.gru_hidden, &h->g0[j], &h->g1[j]);
+  }
   h->have_weights = false;  // fc2 / lm_head must be given again as this rank's rows
   return DD_OK;
 }
@@ -935,8 +1015,9 @@ int dd_destroy(dd_handle* h) {
   int prev = 0;
   cudaGetDevice(&prev);
   cudaSetDevice(h->device);
-  void* ptrs[] = {h->zbuf,     h->midbuf,   h->hbuf[0], h->hbuf[1], h->ghbuf, h->slots,  h->partials,
-                  h->counters, h->status,  h->xbuf,    h->xseq,    h->xdone, h->vwords, h->vdone};
+  // (midbuf and ghbuf live inside xbuf)
+  void* ptrs[] = {h->zbuf,   h->hbuf[0], h->hbuf[1], h->slots,  h->partials, h->counters, h->status,
+                  h->xbuf,   h->xseq,    h->xdone,   h->xsdone, h->vwords,   h->vdone};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   free_packed(h);

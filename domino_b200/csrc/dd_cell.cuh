@@ -150,6 +150,79 @@ __global__ void __launch_bounds__(128) accept_kernel(const int64_t* verify, cons
   bonus[b] = q[a];
 }
 
+// Sharded s / gh phase, gather side: wait (bounded) until every other rank
+// has raised its flag for step `slot`, then copy that rank's column slices of
+// mid (rows 0 .. mid_rows-1, columns [e0[j], e1[j])) and gh (rows 0 .. B-1,
+// columns [g0[j], g1[j])) from its buffers (peer loads over NVLink) into
+// this rank's.  Slice bounds are multiples of 128 elements (16-byte vectors).
+struct GatherParams {
+  Exchange xchg;
+  const unsigned long long* xbuf;  // this rank's exchange buffer (flags)
+  int slot;
+  int mid_rows, E, G3, B;
+  int e0[kMaxRanks], e1[kMaxRanks], g0[kMaxRanks], g1[kMaxRanks];
+  int with_gh;
+  unsigned int* status;
+};
+
+__global__ void __launch_bounds__(256) gather_slices_kernel(const GatherParams p) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const Exchange& x = p.xchg;
+  const unsigned long long seq = *x.seq;
+  const int par = (int)(seq & 1ull);
+  // vectors of 8 elements per (peer, row, column-chunk)
+  long long total = 0;
+  long long mid_n[kMaxRanks], gh_n[kMaxRanks];
+  for (int j = 0; j < x.world; ++j) {
+    mid_n[j] = (j == x.rank) ? 0 : (long long)p.mid_rows * ((p.e1[j] - p.e0[j]) / 8);
+    gh_n[j] = (j == x.rank || !p.with_gh) ? 0 : (long long)p.B * ((p.g1[j] - p.g0[j]) / 8);
+    total += mid_n[j] + gh_n[j];
+  }
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long k = i;
+    int j = 0;
+    while (k >= mid_n[j] + gh_n[j]) {
+      k -= mid_n[j] + gh_n[j];
+      ++j;
+    }
+    // rank j's slices are complete once its flag for this step is raised
+    const unsigned long long* f = p.xbuf + x.sflag_off + ((size_t)par * x.nslots + p.slot) * x.world + j;
+    const uint64_t t0 = globaltimer_ns();
+    bool ok = true;
+    while (true) {
+      unsigned long long v;
+      asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(f) : "memory");
+      if (v == seq) break;
+      if (globaltimer_ns() - t0 > x.timeout_ns) {
+        atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
+        ok = false;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (!ok) continue;
+    const uint8_t* src_base = reinterpret_cast<const uint8_t*>(x.peer[j]);
+    uint8_t* dst_base = reinterpret_cast<uint8_t*>(const_cast<unsigned long long*>(p.xbuf));
+    size_t off;
+    if (k < mid_n[j]) {
+      const int per_row = (p.e1[j] - p.e0[j]) / 8;
+      const long long row = k / per_row;
+      const int c = (int)(k - row * per_row);
+      off = x.mid_off + ((size_t)row * p.E + p.e0[j] + c * 8) * 2;
+    } else {
+      k -= mid_n[j];
+      const int per_row = (p.g1[j] - p.g0[j]) / 8;
+      const long long row = k / per_row;
+      const int c = (int)(k - row * per_row);
+      off = x.gh_off + ((size_t)row * p.G3 + p.g0[j] + c * 8) * 2;
+    }
+    const uint4 v = __ldcv(reinterpret_cast<const uint4*>(src_base + off));
+    *reinterpret_cast<uint4*>(dst_base + off) = v;
+  }
+}
+
 // Greedy verify fused with acceptance (code/dflash.py:472-485):
 // posterior[b, j] = argmax_v logits[b, j, v] (lowest index on ties) and the
 // acceptance of verify[b, :] against it, in one pass over the logits.

@@ -75,6 +75,11 @@ struct Exchange {
   unsigned int* done;                      // per-slot count of finished CTAs (local)
   int nslots, B;
   unsigned long long timeout_ns;
+  // Sharded s / gh phase: rank j raises sflags[(par * nslots + slot) * world + j]
+  // (at u64 offset sflag_off of every buffer) once its slices of mid (byte
+  // offset mid_off) and gh (gh_off) for that step are written.
+  size_t sflag_off, mid_off, gh_off;
+  unsigned int* sdone;  // per-slot finished-CTA counters of the s / gh phase (local)
 };
 
 __device__ __forceinline__ size_t xchg_word(const Exchange& x, int par, int slot, int writer, int b) {
@@ -85,9 +90,10 @@ __device__ __forceinline__ size_t xchg_flag(const Exchange& x, int par, int slot
 }
 
 struct GemvSeg {
-  int rows;
+  int rows;     // rows of W this phase streams
   int tiles;
   int kind;
+  int row_off;  // W row (and output index) of the segment's first row; a multiple of 128
 };
 
 struct GemvParams {
@@ -144,6 +150,7 @@ struct GemvParams {
   long long base_ld, base_out_ld, base_voff;
   Exchange xchg;
   int xslot0, xslot1;  // argmax words this launch publishes to every rank
+  int sflag_slot;      // >= 0: this s / gh launch raises its step flag on every rank when done
 };
 
 __device__ __forceinline__ long long unit_begin(int c, long long U, int G) { return (long long)c * U / G; }
@@ -449,6 +456,32 @@ __global__ void __launch_bounds__(256) pack_tiles_kernel(const uint16_t* __restr
   }
 }
 
+// Sharded s / gh phase: once every CTA of this rank has written its tiles
+// (mid hi/lo rows and gh of this rank's row slices), the last CTA raises this
+// rank's flag for the step in every rank's exchange buffer.
+__device__ __forceinline__ void publish_slices_done(const GemvParams& p, int ept, volatile int* flag) {
+  const Exchange& x = p.xchg;
+  named_bar_sync(1, 128);
+  if (ept == 0) {
+    __threadfence_system();  // this CTA's mid / gh stores, before it is counted
+    const unsigned int old = atomicAdd(x.sdone + p.sflag_slot, 1u);
+    const int last = old == gridDim.x - 1;
+    if (last) {
+      x.sdone[p.sflag_slot] = 0u;
+      __threadfence_system();
+    }
+    *flag = last;
+  }
+  named_bar_sync(1, 128);
+  if (!*flag) return;
+  const unsigned long long seq = *x.seq;
+  const int par = (int)(seq & 1ull);
+  for (int j = ept; j < x.world; j += 128) {
+    unsigned long long* f = x.peer[j] + x.sflag_off + ((size_t)par * x.nslots + p.sflag_slot) * x.world + x.rank;
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(seq) : "memory");
+  }
+}
+
 template <typename T, int kPhase>
 __global__ void __launch_bounds__(kThreads, 2)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
@@ -526,14 +559,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       // loops below advance (tile, kc) and the ring position incrementally.
       auto load_a = [&](int stage, long long tile, int kc) {
         const bool s1 = tile >= p.seg[0].tiles;
-        const long long seg_tile = s1 ? tile - p.seg[0].tiles : tile;
+        const GemvSeg& sg = p.seg[s1 ? 1 : 0];
+        const long long w_tile = (s1 ? tile - p.seg[0].tiles : tile) + sg.row_off / kTileM;
         const uint8_t* pk = p.packed[s1 ? 1 : 0];
         if (pk) {
-          bulk_load(ring + (size_t)stage * p.stage_bytes, pk + (size_t)(seg_tile * KC + kc) * kATileBytes,
+          bulk_load(ring + (size_t)stage * p.stage_bytes, pk + (size_t)(w_tile * KC + kc) * kATileBytes,
                     kATileBytes, &full[stage], pol_w);
         } else {
           tma_load_2d(ring + (size_t)stage * p.stage_bytes, s1 ? &tmA1 : &tmA0, &full[stage], kc * kChunkK,
-                      (int)(seg_tile * kTileM), pol_w);
+                      (int)(w_tile * kTileM), pol_w);
         }
       };
       auto load_b = [&](int stage, int kc) {
@@ -650,8 +684,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 
       const bool s1 = tile >= p.seg[0].tiles;
       const GemvSeg& sg = p.seg[s1 ? 1 : 0];
-      const int row = (int)((s1 ? tile - p.seg[0].tiles : tile) * kTileM) + r;
-      const bool valid = row < sg.rows;
+      const int local_row = (int)((s1 ? tile - p.seg[0].tiles : tile) * kTileM) + r;
+      const bool valid = local_row < sg.rows;
+      const int row = sg.row_off + local_row;
 
       AccView a;
       a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N * p.nacc);
@@ -713,6 +748,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       // contains named barriers).
       if (p.xchg.world > 1 && p.xslot1 > p.xslot0 && named_bar_and(1, 128, *abort_flag == 0))
         publish_words(p, ept, fin_flag);
+    }
+    if constexpr (kPhase == PH_SGH) {
+      if (p.xchg.world > 1 && p.sflag_slot >= 0 && named_bar_and(1, 128, *abort_flag == 0))
+        publish_slices_done(p, ept, fin_flag);
     }
   }
 

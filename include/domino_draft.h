@@ -161,6 +161,9 @@ int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch
  * next kernel on each rank takes the maximum over ranks.  This is the
  * all-reduce(max) on packed (logit, index) words that BASELINE.json's
  * north star describes, fused into the kernels (no separate collective).
+ * The s / gh projections (W_s, W_hh) are split by 128-row slices too: each
+ * rank computes its slice, raises a flag in every rank's buffer, and a small
+ * gather kernel copies the other ranks' slices in over NVLink.
  *
  * Setup per rank: dd_create -> dd_get_exchange_buffer -> dd_ipc_export ->
  * (exchange the 64-byte handles between processes, e.g. all_gather) ->
@@ -211,6 +214,7 @@ int dd_verify_accept(dd_handle* h, const void* target_logits, int32_t logits_dty
 #define DD_PHASE_FC2 5    /* fc2 contraction + base logits + argmax */
 #define DD_PHASE_TABLE 6  /* embed @ W_ih^T table */
 #define DD_PHASE_CELL 7   /* token pick + GRU cell */
+#define DD_PHASE_GATHER 8 /* vocab sharding: other ranks' s / gh slices copied in */
 
 /* Benchmarking aid (no counterpart in the reference): while enabled, the
  * handle records a CUDA event pair around every kernel it launches on the
