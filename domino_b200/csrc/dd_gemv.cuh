@@ -328,13 +328,25 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     for (int ch = 0; ch < nchunks; ++ch) {
       float v[16];
       acc_chunk(a, ch, v);
+      // All z loads of the chunk first: the mid stores below could alias
+      // them, so the compiler would otherwise serialise one L2 round trip
+      // per batch row.
+      float zv[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int b = ch * 16 + j;
+        zv[j] = 0.0f;
+        if (b < p.B && valid) {
+          const size_t zrow = (size_t)b * p.z_rows_per_b + p.z_pos_off + p.t;
+          zv[j] = IO::load((const T*)p.z_src + zrow * p.E + row);
+        }
+      }
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int b = ch * 16 + j;
         if (b < p.B && valid) {
           const float s = IO::to_f(IO::from_f(v[j]));
-          const size_t zrow = (size_t)b * p.z_rows_per_b + p.z_pos_off + p.t;
-          const float z = IO::load((const T*)p.z_src + zrow * p.E + row);
+          const float z = zv[j];
           const float pre = z + s;
           const float mid = pre * sigmoidf_(pre);
           const T hi = IO::from_f(mid);
@@ -352,19 +364,36 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     for (int ch = 0; ch < 4; ++ch)
       if (ch < nchunks) acc_chunk(a, ch, vals + ch * 16);
     const float bias = (valid && p.fc2_bias) ? IO::load((const T*)p.fc2_bias + row) : 0.0f;
+    // Groups of 8 batch rows: their base-logit loads are issued together,
+    // then the 8 independent warp reductions run.
 #pragma unroll
-    for (int b = 0; b < kMaxBatch; ++b) {
-      if (b < p.B) {
-        unsigned long long key = 0ull;
-        if (valid) {
-          const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
-          float logit = vals[2 * b] + vals[2 * b + 1];
-          logit += bias;
-          logit += IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
-          if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
+    for (int b0 = 0; b0 < kMaxBatch; b0 += 8) {
+      if (b0 < p.B) {
+        float basev[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int b = b0 + i;
+          basev[i] = 0.0f;
+          if (b < p.B && valid) {
+            const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
+            basev[i] = IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+          }
         }
-        key = warp_max_u64(key);
-        if (lane == 0) red[q * kMaxBatch + b] = key;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int b = b0 + i;
+          if (b < p.B) {
+            unsigned long long key = 0ull;
+            if (valid) {
+              float logit = vals[2 * b] + vals[2 * b + 1];
+              logit += bias;
+              logit += basev[i];
+              if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
+            }
+            key = warp_max_u64(key);
+            if (lane == 0) red[q * kMaxBatch + b] = key;
+          }
+        }
       }
     }
     named_bar_sync(1, 128);
