@@ -30,9 +30,9 @@ EXPORTS = (
     "dd_accept", "dd_get_status", "dd_last_error", "dd_version", "dd_destroy",
     "dd_set_timing", "dd_read_timing", "dd_rollout_noalloc",
     "dd_get_exchange_buffer", "dd_ipc_export", "dd_ipc_open", "dd_ipc_close", "dd_set_vocab_shard",
-    "dd_set_exchange_timeout", "dd_verify_accept", "dd_set_weight_layout",
+    "dd_set_exchange_timeout", "dd_verify_accept", "dd_set_weight_layout", "dd_set_rollout_mode",
 )
-PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell", 8: "gather"}
+PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell", 8: "gather", 9: "rollout"}
 
 
 class DDConfig(ctypes.Structure):
@@ -106,6 +106,7 @@ def load() -> ctypes.CDLL:
         lib.dd_set_exchange_timeout.argtypes = [vp, ctypes.c_uint64]
         lib.dd_verify_accept.argtypes = [vp, vp, i32, i32, vp, vp, vp, vp, vp]
         lib.dd_set_weight_layout.argtypes = [vp, ctypes.c_int]
+        lib.dd_set_rollout_mode.argtypes = [vp, ctypes.c_int]
         lib.dd_read_timing.argtypes = [vp, vp, vp, i32]
         for name in EXPORTS:
             if name not in ("dd_last_error", "dd_version"):

@@ -31,6 +31,7 @@
 #include "../../include/domino_draft.h"
 #include "dd_cell.cuh"
 #include "dd_gemv.cuh"
+#include "dd_rollout.cuh"
 
 using namespace dd;
 
@@ -114,6 +115,10 @@ struct dd_handle {
   void* pk_fc2 = nullptr;
   void* pk_whh = nullptr;
   void* pk_lm = nullptr;
+  // Persistent rollout (rollout_kernel): per-phase arrival counters + the
+  // device-wide abort word; mode 0 = persistent when supported, 1 = phased.
+  unsigned int* rbar = nullptr;
+  int rollout_mode = 0;
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
@@ -564,6 +569,175 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
   return DD_OK;
 }
 
+// The rollout as one persistent cooperative kernel (dd_rollout.cuh); the same
+// phases, in the same order, as run_rollout launches one by one.  Returns
+// DD_EUNSUPPORTED (and launches nothing) when the handle or the shapes need
+// the phased path: vocab sharding, more phases than the table holds, or a
+// device that cannot keep every CTA resident.
+template <typename T>
+int run_rollout_persistent(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, int npre, int positions,
+                           const void* base, long long base_ld, long long base_voff, int64_t* out, int out_ld,
+                           int out_col0, int64_t* prefix_out, cudaStream_t st) {
+  const dd_config& c = h->cfg;
+  const int n_prefix_total = n_prefix_ids + npre;
+  const int nphases = 1 + 2 * (n_prefix_total - 1) + 3 * c.steps;
+  if (h->rollout_mode != 0 || h->world > 1 || nphases > kMaxRollPhases) return DD_EUNSUPPORTED;
+  static RollParams rp;  // ~10 KB: kept off the stack; the handle is not thread-safe anyway
+  memset(&rp, 0, sizeof(rp));
+  GemvParams& gp = rp.gp;
+  gp = base_params(h);
+  gp.npre = npre;
+  gp.base_src = base;
+  gp.base_rows_per_b = positions;
+  gp.base_pos_off = npre;
+  gp.base_ld = base_ld;
+  gp.base_voff = base_voff;
+  gp.fc2_bias = h->w.fc2_bias;
+  gp.z_src = h->zbuf;
+  gp.z_rows_per_b = positions;
+  gp.z_pos_off = npre;
+  gp.mid_out = h->midbuf;
+  gp.gh_out = h->ghbuf;
+  gp.b_hh = h->w.b_hh;
+  gp.partials = h->partials;
+  gp.tile_counters = h->counters;
+  gp.status = h->status;
+  gp.acc_slots = 2;
+  gp.nacc = 1;
+  CellParams& cp = rp.cp;
+  cp.B = c.batch;
+  cp.G = c.gru_hidden;
+  cp.V = c.vocab;
+  cp.ids = ids;
+  cp.ids_ld = ids_ld;
+  cp.slots = h->slots;
+  cp.nslots = h->nslots;
+  cp.out = out;
+  cp.out_ld = out_ld;
+  cp.table = h->w.table;
+  cp.table_ld = h->w.table_ld;
+  cp.gh = h->ghbuf;
+  cp.b_hh = h->w.b_hh;
+  cp.status = h->status;
+  rp.hbuf[0] = h->hbuf[0];
+  rp.hbuf[1] = h->hbuf[1];
+  rp.bar = h->rbar;
+  rp.abort_word = h->rbar + kMaxRollPhases;
+  rp.ab_fmt = c.dtype == DD_FP16 ? 0u : 1u;
+  const int G3 = 3 * c.gru_hidden;
+  auto gemv = [&](RollPhase& P, int nseg, GemvSeg s0, GemvSeg s1, int a0, int a1, int bmap, int K, int N, int nv,
+                  int t) {
+    P.type = RP_GEMV;
+    P.nseg = nseg;
+    s0.tiles = ceil_div(s0.rows, kTileM);
+    s1.tiles = nseg > 1 ? ceil_div(s1.rows, kTileM) : 0;
+    P.seg[0] = s0;
+    P.seg[1] = s1;
+    P.a_map[0] = a0;
+    P.a_map[1] = a1;
+    P.b_map = bmap;
+    P.K = K;
+    P.KC = ceil_div(K, kChunkK);
+    P.N = N;
+    P.n_valid = nv;
+    P.t = t;
+  };
+  // Prefix tokens are written only by dd_draft_block, into the same array.
+  if (prefix_out != nullptr && prefix_out != out) return DD_EUNSUPPORTED;
+  const bool prefix_writes_out = prefix_out != nullptr;
+  int n = 0, cur = 0;
+  {
+    RollPhase& P = rp.ph[n++];
+    P.type = RP_CELL;
+    P.src = 0;
+    P.ids_col = 0;
+    P.out_col = prefix_writes_out ? 0 : -1;
+    P.h_zero = 1;
+    P.write_h = 1;
+    P.h_out = 0;
+  }
+  for (int j = 1; j < n_prefix_total; ++j) {
+    gemv(rp.ph[n++], 1, GemvSeg{G3, 0, EPI_GH, 0}, GemvSeg{0, 0, 0, 0}, 1, 1, cur, c.gru_hidden, h->N1, c.batch, 0);
+    RollPhase& P = rp.ph[n++];
+    P.type = RP_CELL;
+    if (j < n_prefix_ids) {
+      P.src = 0;
+      P.ids_col = j;
+      P.out_col = -1;
+    } else {
+      P.src = 1;
+      P.slot_idx = j - n_prefix_ids;
+      P.out_col = prefix_writes_out ? j : -1;
+    }
+    P.write_h = 1;
+    P.h_in = cur;
+    P.h_out = cur ^ 1;
+    cur ^= 1;
+  }
+  for (int t = 0; t < c.steps; ++t) {
+    const bool last = t + 1 == c.steps;
+    gemv(rp.ph[n++], last ? 1 : 2, GemvSeg{c.emb_dim, 0, EPI_SPROJ_MID, 0}, GemvSeg{G3, 0, EPI_GH, 0}, 0, 1, cur,
+         c.gru_hidden, h->N1, c.batch, t);
+    gemv(rp.ph[n++], 1, GemvSeg{h->v_local, 0, EPI_FC2_ARGMAX, 0}, GemvSeg{0, 0, 0, 0}, 2, 2, 2, c.emb_dim, h->N2,
+         2 * c.batch, t);
+    RollPhase& P = rp.ph[n++];
+    P.type = RP_CELL;
+    P.src = 1;
+    P.slot_idx = npre + t;
+    P.out_col = out_col0 + t;
+    P.write_h = last ? 0 : 1;
+    P.h_in = cur;
+    P.h_out = cur ^ 1;
+    cur ^= 1;
+  }
+  rp.nphases = n;
+  int tiles_max = 0;
+  for (int i = 0; i < n; ++i)
+    if (rp.ph[i].type == RP_GEMV) tiles_max = std::max(tiles_max, rp.ph[i].seg[0].tiles + rp.ph[i].seg[1].tiles);
+  if (tiles_max > h->max_tiles) return fail(h, DD_EINVAL, "rollout phase has %d tiles > %d", tiles_max, h->max_tiles);
+  // launch shape: one ring layout sized for the wider activation operand
+  rp.n_max = std::max(h->N1, h->N2);
+  rp.stage_bytes = kATileBytes + (uint32_t)rp.n_max * 128u;
+  rp.stages = std::max(4, std::min<int>(kMaxStages, (int)((uint32_t)h->ring_kb_big * 1024u / rp.stage_bytes)));
+  uint32_t cols = 32;
+  while (cols < (uint32_t)(2 * rp.n_max)) cols <<= 1;
+  rp.tmem_cols = cols;
+  const size_t smem = 1024 + (size_t)rp.stages * rp.stage_bytes + kSmemTail;
+  static bool attr_done[64][2] = {};
+  const int ti = std::is_same<T, __half>::value ? 1 : 0;
+  if (!attr_done[h->device & 63][ti]) {
+    DD_CUDA(h, cudaFuncSetAttribute(rollout_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_done[h->device & 63][ti] = true;
+  }
+  int per_sm = 0;
+  DD_CUDA(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rollout_kernel<T>, kThreads, smem));
+  if (per_sm < 1) return DD_EUNSUPPORTED;
+  const int grid = h->num_sms * std::min(per_sm, h->ctas_per_sm_big);
+  if (grid > h->max_ctas) return DD_EUNSUPPORTED;
+  RollMaps maps;
+  maps.a[0] = h->tm_ws;
+  maps.a[1] = h->tm_whh;
+  maps.a[2] = h->tm_fc2;
+  maps.b[0] = h->tm_h[0];
+  maps.b[1] = h->tm_h[1];
+  maps.b[2] = h->tm_mid;
+  DD_CUDA(h, cudaMemsetAsync(h->rbar, 0, (size_t)(kMaxRollPhases + 1) * 4, st));
+  int rc = timing_begin(h, DD_PHASE_ROLLOUT, st);
+  if (rc) return rc;
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the phases wait on one another
+  attr[0].val.cooperative = 1;
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  DD_CUDA(h, cudaLaunchKernelEx(&cfg, rollout_kernel<T>, maps, rp));
+  return timing_end(h, st);
+}
+
 // The library links its own (static) CUDA runtime, whose current device is
 // private to it: every entry point selects the handle's device itself.
 int use_device(dd_handle* h) {
@@ -659,6 +833,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", h->ctas_per_sm_small, 1, 2);
   h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
   h->pack = env_int("DD_PACK_WEIGHTS", 0, 0, 1) != 0;
+  h->rollout_mode = env_int("DD_ROLLOUT_PHASED", 0, 0, 1);
   h->max_nacc = env_int("DD_NACC", h->max_nacc, 1, 4);
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", h->tmem_cols_per_cta, 32, 512);
   int prev = 0;
@@ -688,6 +863,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
       {(void**)&h->xdone, (size_t)h->nslots * 4},
       {(void**)&h->vwords, (size_t)c.batch * dd_handle::kMaxVerifyPositions * 8},
       {(void**)&h->vdone, 64},
+      {(void**)&h->rbar, (size_t)(kMaxRollPhases + 1) * 4},
   };
   for (auto& a : allocs) {
     if (cudaMalloc(a.p, a.bytes) != cudaSuccess)
@@ -749,6 +925,12 @@ int dd_set_weights(dd_handle* h, const dd_weights* w) {
   return DD_OK;
 }
 
+int dd_set_rollout_mode(dd_handle* h, int mode) {
+  if (!h || mode < 0 || mode > 1) return DD_EINVAL;
+  h->rollout_mode = mode;
+  return DD_OK;
+}
+
 int dd_set_weight_layout(dd_handle* h, int packed) {
   if (!h) return DD_EINVAL;
   h->pack = packed != 0;
@@ -803,11 +985,17 @@ int dd_rollout(dd_handle* h, const int64_t* prefix_ids, const void* parallel_hid
   if (c.dtype == DD_FP16) {
     rc = run_z_phase<__half>(h, parallel_hiddens, c.steps, 0, nullptr, st);
     if (!rc)
+      rc = run_rollout_persistent<__half>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits,
+                                          ld, voff, out_tokens, c.steps, 0, nullptr, st);
+    if (rc == DD_EUNSUPPORTED)
       rc = run_rollout<__half>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, ld, voff,
                                out_tokens, c.steps, 0, nullptr, st);
   } else {
     rc = run_z_phase<__nv_bfloat16>(h, parallel_hiddens, c.steps, 0, nullptr, st);
     if (!rc)
+      rc = run_rollout_persistent<__nv_bfloat16>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps,
+                                                 base_logits, ld, voff, out_tokens, c.steps, 0, nullptr, st);
+    if (rc == DD_EUNSUPPORTED)
       rc = run_rollout<__nv_bfloat16>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, ld,
                                       voff, out_tokens, c.steps, 0, nullptr, st);
   }
@@ -833,11 +1021,17 @@ int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel
   if (c.dtype == DD_FP16) {
     rc = run_z_phase<__half>(h, parallel_hiddens, positions, npre, base_logits_out, st);
     if (!rc)
+      rc = run_rollout_persistent<__half>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out,
+                                          ld, 1 + npre, verify_out, st);
+    if (rc == DD_EUNSUPPORTED)
       rc = run_rollout<__half>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out, ld,
                                1 + npre, verify_out, st);
   } else {
     rc = run_z_phase<__nv_bfloat16>(h, parallel_hiddens, positions, npre, base_logits_out, st);
     if (!rc)
+      rc = run_rollout_persistent<__nv_bfloat16>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0,
+                                                 verify_out, ld, 1 + npre, verify_out, st);
+    if (rc == DD_EUNSUPPORTED)
       rc = run_rollout<__nv_bfloat16>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out,
                                       ld, 1 + npre, verify_out, st);
   }
@@ -1016,8 +1210,8 @@ int dd_destroy(dd_handle* h) {
   cudaGetDevice(&prev);
   cudaSetDevice(h->device);
   // (midbuf and ghbuf live inside xbuf)
-  void* ptrs[] = {h->zbuf,   h->hbuf[0], h->hbuf[1], h->slots,  h->partials, h->counters, h->status,
-                  h->xbuf,   h->xseq,    h->xdone,   h->xsdone, h->vwords,   h->vdone};
+  void* ptrs[] = {h->zbuf, h->hbuf[0], h->hbuf[1], h->slots,  h->partials, h->counters, h->status,
+                  h->xbuf, h->xseq,    h->xdone,   h->xsdone, h->vwords,   h->vdone,    h->rbar};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   free_packed(h);

@@ -66,13 +66,11 @@ __device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
   for (int i = 0; i < 8; ++i) f[i] = io<T>::to_f(e[i]);
 }
 
+// One thread's share of a GRU step: 8 state elements of one batch row
+// (idx < B * G / 8).
 template <typename T>
-__global__ void __launch_bounds__(128) cell_kernel(const CellParams p) {
-  pdl_launch_dependents();
-  pdl_wait_primary();
+__device__ __forceinline__ void cell_apply(const CellParams& p, int idx) {
   const int per_row = p.G / 8;
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= p.B * per_row) return;
   const int b = idx / per_row;
   const int g0 = (idx - b * per_row) * 8;
 
@@ -131,6 +129,15 @@ __global__ void __launch_bounds__(128) cell_kernel(const CellParams p) {
   }
   *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h_out) + (size_t)b * G + g0) =
       *reinterpret_cast<const uint4*>(outv);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) cell_kernel(const CellParams p) {
+  pdl_launch_dependents();
+  pdl_wait_primary();
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= p.B * (p.G / 8)) return;
+  cell_apply<T>(p, idx);
 }
 
 // accept[b] = number of leading draft tokens equal to the target's greedy

@@ -153,9 +153,15 @@ struct GemvParams {
   int sflag_slot;      // >= 0: this s / gh launch raises its step flag on every rank when done
 };
 
-__device__ __forceinline__ long long unit_begin(int c, long long U, int G) { return (long long)c * U / G; }
+// CTA c's units are [unit_begin(c), unit_begin(c + 1)): equal contiguous
+// ranges when there are at least as many units as CTAs; otherwise one unit
+// each for the first U CTAs, so that CTAs without work only come last.
+__device__ __forceinline__ long long unit_begin(int c, long long U, int G) {
+  return U >= G ? (long long)c * U / G : (c < U ? c : U);
+}
 
 __device__ __forceinline__ int cta_of_unit(long long u, long long U, int G) {
+  if (U < G) return (int)u;
   int c = (int)((u * G) / U);
   if (c >= G) c = G - 1;
   while (c + 1 < G && unit_begin(c + 1, U, G) <= u) ++c;
@@ -254,7 +260,7 @@ __device__ __forceinline__ void acc_chunk(const AccView& a, int ch, float* v) {
 
 // Phases (one kernel instantiation each, so profiles attribute time per
 // phase); kPhase also prunes the epilogues a phase cannot use.
-enum Phase : int { PH_Z = 1, PH_ZLM = 2, PH_GH = 3, PH_SGH = 4, PH_FC2 = 5, PH_TABLE = 6 };
+enum Phase : int { PH_Z = 1, PH_ZLM = 2, PH_GH = 3, PH_SGH = 4, PH_FC2 = 5, PH_TABLE = 6, PH_ALL = 7 };
 
 template <int kPhase>
 __device__ __forceinline__ constexpr bool phase_has(int kind) {
@@ -265,6 +271,7 @@ __device__ __forceinline__ constexpr bool phase_has(int kind) {
     case PH_SGH: return kind == EPI_SPROJ_MID || kind == EPI_GH;
     case PH_FC2: return kind == EPI_FC2_ARGMAX;
     case PH_TABLE: return kind == EPI_TABLE;
+    case PH_ALL: return true;
   }
   return false;
 }

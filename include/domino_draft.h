@@ -90,6 +90,13 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out);
  * it synchronises the device).  Call again after the weights change. */
 int dd_set_weights(dd_handle* h, const dd_weights* w);
 
+/* How dd_rollout / dd_draft_block run the rollout after the z projection:
+ * 0 (default) one persistent cooperative kernel for all prefix and draft
+ * steps when the handle allows it (unsharded, at most 64 phases), else one
+ * kernel per phase; 1 always one kernel per phase.  DD_ROLLOUT_PHASED=1 in
+ * the environment selects 1 at dd_create.  Both give identical tokens. */
+int dd_set_rollout_mode(dd_handle* h, int mode);
+
 /* packed = 0 (default: stream the caller's row-major weights in place, no
  * extra memory) or 1 (stream the packed copy with 1-D bulk copies; measured
  * equal speed at the default launch shape; DD_PACK_WEIGHTS=1 in the
@@ -215,6 +222,7 @@ int dd_verify_accept(dd_handle* h, const void* target_logits, int32_t logits_dty
 #define DD_PHASE_TABLE 6  /* embed @ W_ih^T table */
 #define DD_PHASE_CELL 7   /* token pick + GRU cell */
 #define DD_PHASE_GATHER 8 /* vocab sharding: other ranks' s / gh slices copied in */
+#define DD_PHASE_ROLLOUT 9 /* the whole rollout as one persistent kernel */
 
 /* Benchmarking aid (no counterpart in the reference): while enabled, the
  * handle records a CUDA event pair around every kernel it launches on the

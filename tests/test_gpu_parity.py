@@ -6,6 +6,8 @@ history (teacher forcing), or the oracle's logit of that token is within
 2e-2 (abs + rel) of its top logit (a near-tie).  Integer outputs
 (acceptance, bonus tokens, prefix tokens over identical logits) are exact.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -138,6 +140,45 @@ def test_packed_and_row_major_weights_agree_exactly(B, P):
     vr, br = rr.draft_block(last, ph2)
     assert torch.equal(vp, vr) and torch.equal(bp, br)
     assert rp.status() == 0 and rr.status() == 0
+
+
+@pytest.mark.parametrize("B,H,G,E,V,S,P", [
+    (1, 128, 128, 192, 1500, 15, 1),
+    (3, 256, 192, 320, 3001, 13, 3),
+    (8, 128, 64, 136, 2000, 15, 1),
+    (17, 64, 64, 96, 1000, 15, 2),
+])
+def test_persistent_rollout_matches_phased_exactly(B, H, G, E, V, S, P):
+    """The one-kernel rollout and the kernel-per-phase rollout split the work
+    the same way, so their tokens are identical."""
+    from domino_b200 import _lib
+
+    draft, target = random_modules(H, G, E, V, seed=90 + B, fc2_std=0.08, fc1_bias=True, gru_bias=True)
+    rp = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    rk = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    lib = _lib.load()
+    assert lib.dd_set_rollout_mode(rk._h, 1) == _lib.DD_OK
+    for seed in range(2):
+        prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=seed)
+        a = rp(prefix, ph, base)
+        b = rk(prefix, ph, base)
+        assert torch.equal(a, b), (a, b)
+    K = P - 1 + S
+    g = torch.Generator().manual_seed(5)
+    ph2 = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    last = torch.randint(0, V, (B,), generator=g).cuda()
+    va, ba = rp.draft_block(last, ph2)
+    vb, bb = rk.draft_block(last, ph2)
+    assert torch.equal(va, vb) and torch.equal(ba, bb)
+    assert rp.status() == 0 and rk.status() == 0
+    # and the persistent path is the one that ran
+    lib.dd_set_timing(rp._h, 1)
+    rp(prefix, ph, base)
+    kinds = (ctypes.c_int32 * 64)()
+    ms = (ctypes.c_float * 64)()
+    n = lib.dd_read_timing(rp._h, kinds, ms, 64)
+    lib.dd_set_timing(rp._h, 0)
+    assert 9 in list(kinds[:n]), list(kinds[:n])
 
 
 def test_draft_block_fused_lm_head():
