@@ -116,9 +116,10 @@ struct dd_handle {
   void* pk_whh = nullptr;
   void* pk_lm = nullptr;
   // Persistent rollout (rollout_kernel): per-phase arrival counters + the
-  // device-wide abort word; mode 0 = persistent when supported, 1 = phased.
+  // device-wide abort word; mode 0 = persistent when supported, 1 = phased
+  // (default: measured faster on B200).
   unsigned int* rbar = nullptr;
-  int rollout_mode = 0;
+  int rollout_mode = 1;
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
@@ -695,14 +696,20 @@ int run_rollout_persistent(dd_handle* h, const int64_t* ids, int ids_ld, int n_p
   for (int i = 0; i < n; ++i)
     if (rp.ph[i].type == RP_GEMV) tiles_max = std::max(tiles_max, rp.ph[i].seg[0].tiles + rp.ph[i].seg[1].tiles);
   if (tiles_max > h->max_tiles) return fail(h, DD_EINVAL, "rollout phase has %d tiles > %d", tiles_max, h->max_tiles);
-  // launch shape: one ring layout sized for the wider activation operand
+  // Launch shape: one CTA per SM holding ctas_per_sm_big pipelines, each with
+  // one ring layout sized for the wider activation operand.
+  rp.subs = h->ctas_per_sm_big;
   rp.n_max = std::max(h->N1, h->N2);
   rp.stage_bytes = kATileBytes + (uint32_t)rp.n_max * 128u;
   rp.stages = std::max(4, std::min<int>(kMaxStages, (int)((uint32_t)h->ring_kb_big * 1024u / rp.stage_bytes)));
+  const int fit = (int)(((227u * 1024u - 1024u) / (uint32_t)rp.subs - kSmemTail) / rp.stage_bytes);
+  rp.stages = std::min(rp.stages, fit);
+  if (rp.stages < 2) return DD_EUNSUPPORTED;
   uint32_t cols = 32;
   while (cols < (uint32_t)(2 * rp.n_max)) cols <<= 1;
   rp.tmem_cols = cols;
-  const size_t smem = 1024 + (size_t)rp.stages * rp.stage_bytes + kSmemTail;
+  const size_t smem = 1024 + (size_t)rp.subs * ((size_t)rp.stages * rp.stage_bytes + kSmemTail);
+  const int threads = rp.subs * kThreads;
   static bool attr_done[64][2] = {};
   const int ti = std::is_same<T, __half>::value ? 1 : 0;
   if (!attr_done[h->device & 63][ti]) {
@@ -710,10 +717,12 @@ int run_rollout_persistent(dd_handle* h, const int64_t* ids, int ids_ld, int n_p
     attr_done[h->device & 63][ti] = true;
   }
   int per_sm = 0;
-  DD_CUDA(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rollout_kernel<T>, kThreads, smem));
+  // The occupancy calculator counts any kernel that allocates TMEM as one
+  // CTA per SM, and a cooperative launch is held to that count.
+  DD_CUDA(h, cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rollout_kernel<T>, threads, smem));
   if (per_sm < 1) return DD_EUNSUPPORTED;
-  const int grid = h->num_sms * std::min(per_sm, h->ctas_per_sm_big);
-  if (grid > h->max_ctas) return DD_EUNSUPPORTED;
+  const int grid = h->num_sms;
+  if (grid * rp.subs > h->max_ctas) return DD_EUNSUPPORTED;
   RollMaps maps;
   maps.a[0] = h->tm_ws;
   maps.a[1] = h->tm_whh;
@@ -729,7 +738,7 @@ int run_rollout_persistent(dd_handle* h, const int64_t* ids, int ids_ld, int n_p
   attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: the phases wait on one another
   attr[0].val.cooperative = 1;
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(threads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -833,7 +842,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", h->ctas_per_sm_small, 1, 2);
   h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
   h->pack = env_int("DD_PACK_WEIGHTS", 0, 0, 1) != 0;
-  h->rollout_mode = env_int("DD_ROLLOUT_PHASED", 0, 0, 1);
+  h->rollout_mode = env_int("DD_ROLLOUT_PERSISTENT", 0, 0, 1) ? 0 : 1;
   h->max_nacc = env_int("DD_NACC", h->max_nacc, 1, 4);
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", h->tmem_cols_per_cta, 32, 512);
   int prev = 0;
@@ -1311,6 +1320,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.v_local = c.vocab;  // unsharded
   h.world = 1;
   h.rank = 0;
+  h.rollout_mode = 1;  // one launch per phase: the persistent kernel's grid counters are not in this scratch
   const int npre_max = c.prefix_tokens - 1;
   h.nslots = npre_max + c.steps;
   h.max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;

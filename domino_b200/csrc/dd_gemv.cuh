@@ -217,6 +217,7 @@ struct AccView {
   int r;               // row within the tile
   long long U;
   int G, KC;
+  uint32_t bar;        // named barrier of the 128 epilogue threads
 };
 
 // This CTA's part of 16 accumulator columns [ch*16, ch*16+16): the sum of the
@@ -403,7 +404,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
         }
       }
     }
-    named_bar_sync(1, 128);
+    named_bar_sync(a.bar, 128);
     if (ept < p.B) {
       unsigned long long k = red[ept];
 #pragma unroll
@@ -413,7 +414,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
       }
       if (k) atomicMax(p.slots + (size_t)ept * p.nslots + p.npre + p.t, k);
     }
-    named_bar_sync(1, 128);
+    named_bar_sync(a.bar, 128);
     return;
   }
 }
@@ -727,6 +728,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       AccView a;
       a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N * p.nacc);
       a.nacc = p.nacc;
+      a.bar = 1;
       a.combine = false;
       a.nseg = 1;
       a.myseg = 0;

@@ -6,7 +6,7 @@
 // (last tile's epilogue and split-tile fix-up) and a launch gap; with the
 // checkpoint-sized correction MLP (E ~ 1k) those fixed costs are about half
 // of every step.  rollout_kernel runs every phase of the rollout in one
-// cooperative launch (all CTAs resident, 2 per SM):
+// cooperative launch (one CTA per SM, two pipelines per CTA, all resident):
 //
 //   * the TMA producer keeps two cursors over this CTA's units of all
 //     phases: the weight cursor runs ahead across phase boundaries as far as
@@ -56,10 +56,11 @@ struct RollParams {
   void* hbuf[2];
   unsigned int* bar;         // [nphases] CTA arrivals per phase; zero at launch
   unsigned int* abort_word;  // device-wide abort; zero at launch
+  int subs;                  // pipelines per CTA (1 or 2)
   int stages;
   uint32_t stage_bytes;      // 16 KB weight tile + n_max * 128 B activation slice
   int n_max;                 // TMEM columns per accumulator slot
-  uint32_t tmem_cols;
+  uint32_t tmem_cols;        // TMEM columns per pipeline
   uint32_t ab_fmt;           // 1 = bf16, 0 = fp16
 };
 
@@ -91,6 +92,9 @@ struct UnitCursor {
   long long u, ue;     // unit and end of this CTA's range in the phase
   long long tile;
   int kc, KC;
+  // the phase's fields the producer needs per unit, read once per phase
+  int tiles0, row_tile0, row_tile1, a0, a1, b_map;
+  uint32_t b_bytes;
 };
 
 __device__ __forceinline__ void cursor_seek(UnitCursor& cu, const RollParams& rp, int from, int c, int G) {
@@ -106,6 +110,13 @@ __device__ __forceinline__ void cursor_seek(UnitCursor& cu, const RollParams& rp
       cu.KC = P.KC;
       cu.tile = b / P.KC;
       cu.kc = (int)(b - cu.tile * P.KC);
+      cu.tiles0 = P.seg[0].tiles;
+      cu.row_tile0 = P.seg[0].row_off / kTileM;
+      cu.row_tile1 = P.seg[1].row_off / kTileM - P.seg[0].tiles;
+      cu.a0 = P.a_map[0];
+      cu.a1 = P.a_map[1];
+      cu.b_map = P.b_map;
+      cu.b_bytes = (uint32_t)P.N * 128u;
       return;
     }
   }
@@ -123,9 +134,10 @@ __device__ __forceinline__ void cursor_next(UnitCursor& cu, const RollParams& rp
 
 // Epilogue warps: wait until every CTA has arrived on `bar` (bounded; gives
 // up at once when the device-wide abort word is set).  Collective over the
-// 128 epilogue threads; true when the phase completed.
+// 128 epilogue threads of one pipeline (named barrier `ebar`); true when the
+// phase completed.
 __device__ __forceinline__ bool grid_wait(const unsigned int* bar, unsigned int target, volatile unsigned int* gabort,
-                                          volatile int* abort_flag, int ept) {
+                                          volatile int* abort_flag, int ept, uint32_t ebar) {
   bool ok = true;
   if (ept == 0) {
     const uint64_t t0 = globaltimer_ns();
@@ -143,17 +155,26 @@ __device__ __forceinline__ bool grid_wait(const unsigned int* bar, unsigned int 
       __nanosleep(64);
     }
   }
-  ok = named_bar_and(1, 128, ok);
+  ok = named_bar_and(ebar, 128, ok);
   __threadfence();
   return ok;
 }
 
+// One CTA per SM holds rp.subs (1 or 2) independent pipelines of kThreads
+// threads each: warp 0 TMA, warp 1 MMA, warps 2..5 epilogue, with their own
+// ring, barriers and TMEM columns.  A cooperative launch admits only one
+// TMEM-allocating CTA per SM, while streaming the weights at full HBM rate
+// takes two pipelines per SM; pipeline s of CTA b acts as CTA
+// s * gridDim.x + b of a grid of rp.subs * gridDim.x.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(2 * kThreads, 1)
     rollout_kernel(const __grid_constant__ RollMaps maps, const __grid_constant__ RollParams rp) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = smem;
+  const int sub = (int)threadIdx.x / kThreads;
+  const int tid = (int)threadIdx.x - sub * kThreads;
+  uint8_t* smem0 = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const size_t sub_bytes = (size_t)rp.stages * rp.stage_bytes + kSmemTail;
+  uint8_t* ring = smem0 + (size_t)sub * sub_bytes;
   uint8_t* tail = ring + (size_t)rp.stages * rp.stage_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(tail);
   uint64_t* empty = full + kMaxStages;
@@ -166,14 +187,18 @@ __global__ void __launch_bounds__(kThreads, 2)
   long long* issued = reinterpret_cast<long long*>(tail + 512);  // [0] weight loads, [2] activation loads
   long long* consumed = issued + 1;
   unsigned long long* red = reinterpret_cast<unsigned long long*>(tail + 1024);
+  // pipeline 0's holder: the one TMEM allocation of the CTA
+  uint32_t* tmem_holder0 = reinterpret_cast<uint32_t*>(smem0 + (size_t)rp.stages * rp.stage_bytes +
+                                                       (size_t)(2 * kMaxStages + 5) * sizeof(uint64_t));
   volatile unsigned int* gabort = rp.abort_word;
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int c = blockIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int G = (int)gridDim.x * rp.subs;
+  const int c = sub * (int)gridDim.x + (int)blockIdx.x;
+  const uint32_t ebar = 1u + (uint32_t)sub;  // named barrier of this pipeline's epilogue warps
 
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     for (int s = 0; s < rp.stages; ++s) {
       mbar_init(&full[s], 2);  // weight tile + activation slice, each with its own expect_tx
       mbar_init(&empty[s], 1);
@@ -190,20 +215,20 @@ __global__ void __launch_bounds__(kThreads, 2)
     *consumed = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) {
+  if (sub == 0 && warp == 0 && lane == 0) {
     for (int i = 0; i < 3; ++i) {
       prefetch_tmap(&maps.a[i]);
       prefetch_tmap(&maps.b[i]);
     }
   }
-  if (warp == 1) {
-    tmem_alloc(tmem_holder, rp.tmem_cols);
+  if (sub == 0 && warp == 1) {
+    tmem_alloc(tmem_holder0, rp.tmem_cols * (uint32_t)rp.subs);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t tmem_base = *tmem_holder0 + (uint32_t)sub * rp.tmem_cols;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -216,55 +241,61 @@ __global__ void __launch_bounds__(kThreads, 2)
       int sa = 0, sb = 0;
       uint32_t pa = 0;
       long long na = 0, nb = 0;
-      int ready_upto = -1;  // phases [0, ready_upto] known complete on every CTA
-      uint64_t last = globaltimer_ns();
+      int ready_upto = -1;       // phases [0, ready_upto] known complete on every CTA
+      uint64_t stall_since = 0;  // read the timer only while nothing can be issued
       while (A.ph < rp.nphases || Bc.ph < rp.nphases) {
-        bool progress = false;
-        if (A.ph < rp.nphases && mbar_test_wait(&empty[sa], pa ^ 1u)) {
-          const RollPhase& P = rp.ph[A.ph];
-          const bool s1 = A.tile >= P.seg[0].tiles;
-          const GemvSeg& sg = P.seg[s1 ? 1 : 0];
-          const long long w_tile = (s1 ? A.tile - P.seg[0].tiles : A.tile) + sg.row_off / kTileM;
-          mbar_arrive_expect_tx(&full[sa], kATileBytes);
-          tma_load_2d(ring + (size_t)sa * rp.stage_bytes, &maps.a[P.a_map[s1 ? 1 : 0]], &full[sa], A.kc * kChunkK,
-                      (int)(w_tile * kTileM), pol_w);
-          cursor_next(A, rp, c, G);
-          ++na;
-          if (++sa == rp.stages) {
-            sa = 0;
-            pa ^= 1u;
-          }
-          progress = true;
-        }
+        // Activation load first: it is what the MMA is waiting for.
+        bool b_blocked = false;
         if (Bc.ph < rp.nphases && nb < na) {
           const int need = Bc.ph - 1;  // the activations come from the phase before
-          bool ready = need <= ready_upto;
-          if (!ready && ld_acquire_u32(rp.bar + need) >= (unsigned int)G) {
+          if (need > ready_upto && ld_acquire_u32(rp.bar + need) >= (unsigned int)G) {
             ready_upto = need;
-            ready = true;
             fence_proxy_async_global();  // generic stores of other CTAs -> this CTA's TMA reads
           }
-          if (ready) {
-            const RollPhase& P = rp.ph[Bc.ph];
-            mbar_arrive_expect_tx(&full[sb], (uint32_t)P.N * 128u);
-            tma_load_2d(ring + (size_t)sb * rp.stage_bytes + kATileBytes, &maps.b[P.b_map], &full[sb],
+          if (need <= ready_upto) {
+            mbar_arrive_expect_tx(&full[sb], Bc.b_bytes);
+            tma_load_2d(ring + (size_t)sb * rp.stage_bytes + kATileBytes, &maps.b[Bc.b_map], &full[sb],
                         Bc.kc * kChunkK, 0, pol_x);
             cursor_next(Bc, rp, c, G);
             ++nb;
             if (++sb == rp.stages) sb = 0;
-            progress = true;
+            stall_since = 0;
+            continue;
+          }
+          b_blocked = true;
+        }
+        if (A.ph < rp.nphases) {
+          // With no activation load pending, park on the ring slot (the
+          // hardware wakes us when it frees); otherwise only test it, so the
+          // grid barrier is polled again.
+          const bool got = b_blocked ? mbar_test_wait(&empty[sa], pa ^ 1u) : mbar_try_wait(&empty[sa], pa ^ 1u);
+          if (got) {
+            const bool s1 = A.tile >= A.tiles0;
+            const long long w_tile = A.tile + (s1 ? A.row_tile1 : A.row_tile0);
+            mbar_arrive_expect_tx(&full[sa], kATileBytes);
+            tma_load_2d(ring + (size_t)sa * rp.stage_bytes, &maps.a[s1 ? A.a1 : A.a0], &full[sa], A.kc * kChunkK,
+                        (int)(w_tile * kTileM), pol_w);
+            cursor_next(A, rp, c, G);
+            ++na;
+            if (++sa == rp.stages) {
+              sa = 0;
+              pa ^= 1u;
+            }
+            stall_since = 0;
+            continue;
           }
         }
-        if (progress) {
-          last = globaltimer_ns();
-        } else {
-          if (*gabort || *abort_flag) break;
-          if (globaltimer_ns() - last > kWaitLimitNs) {
-            *abort_flag = 1;
-            *gabort = 1u;
-            break;
-          }
-          __nanosleep(32);
+        // The device-wide word lives in global memory: a read costs an L2 round
+        // trip, so only a producer that is waiting on the grid anyway looks at
+        // it; otherwise this pipeline's own roles raise the shared-memory flag.
+        if (*abort_flag || (b_blocked && *gabort)) break;
+        const uint64_t now = globaltimer_ns();
+        if (stall_since == 0) {
+          stall_since = now;
+        } else if (now - stall_since > kWaitLimitNs) {
+          *abort_flag = 1;
+          *gabort = 1u;
+          break;
         }
       }
       issued[0] = na;
@@ -328,8 +359,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     // ---------------------------------------- epilogue warps 2..5: tiles, cells, arrivals
-    const int ept = threadIdx.x - kEpiWarp0 * 32;
-    const int q = warp & 3;
+    const int ept = tid - kEpiWarp0 * 32;
+    // TMEM lane quarter: set by the warp's index within the CTA
+    const int q = ((int)threadIdx.x >> 5) & 3;
     const int r = q * 32 + lane;
     int acc_it = 0;
     bool ok = true;
@@ -359,7 +391,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           const int slot = acc_it & 1;
           const uint32_t use = (uint32_t)(acc_it >> 1);
           const bool got = mbar_wait_bounded(&accf[slot], use & 1u, abort_flag);
-          if (!named_bar_and(1, 128, got)) {
+          if (!named_bar_and(ebar, 128, got)) {
             ok = false;
             break;
           }
@@ -383,6 +415,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           a.U = U;
           a.G = G;
           a.KC = KC;
+          a.bar = ebar;
           bool finish = true;
           if (kc0 > 0 || kc1 < KC) {
             const int c_lo = cta_of_unit(tile * KC, U, G);
@@ -398,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               for (int j = 0; j < 16; ++j) __stcg(mine + (size_t)(ch * 16 + j) * kTileM + r, v[j]);
             }
             __threadfence();
-            named_bar_sync(1, 128);
+            named_bar_sync(ebar, 128);
             if (ept == 0) {
               const unsigned int old = atomicAdd(p.tile_counters + tile, 1u);
               const int lastseg = (old == (unsigned int)(a.nseg - 1)) ? 1 : 0;
@@ -408,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 2)
               }
               *fin_flag = lastseg;
             }
-            named_bar_sync(1, 128);
+            named_bar_sync(ebar, 128);
             finish = *fin_flag != 0;
             if (finish) {
               __threadfence();
@@ -425,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       } else {
         // GRU cell over this CTA's slice of batch x state, once the phase
         // before (fc2 argmax, or the prefix gh) has completed everywhere.
-        if (i > 0 && !grid_wait(rp.bar + (i - 1), (unsigned int)G, gabort, abort_flag, ept)) {
+        if (i > 0 && !grid_wait(rp.bar + (i - 1), (unsigned int)G, gabort, abort_flag, ept, ebar)) {
           ok = false;
           break;
         }
@@ -444,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       // This CTA is done with phase i.
       __threadfence();
-      named_bar_sync(1, 128);
+      named_bar_sync(ebar, 128);
       if (ept == 0) atomicAdd(rp.bar + i, 1u);
     }
     if (!ok) {
@@ -469,13 +502,13 @@ __global__ void __launch_bounds__(kThreads, 2)
         wait_ns(f, (uint32_t)((it / rp.stages) & 1), 100ull * 1000 * 1000);
       }
     }
-    if (threadIdx.x == 0) atomicOr(rp.gp.status, 1u /* DD_STATUS_TIMEOUT */);
-    __syncthreads();
+    if (tid == 0) atomicOr(rp.gp.status, 1u /* DD_STATUS_TIMEOUT */);
   }
+  __syncthreads();
   tc_fence_after();
-  if (warp == 1) {
+  if (sub == 0 && warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, rp.tmem_cols);
+    tmem_dealloc(*tmem_holder0, rp.tmem_cols * (uint32_t)rp.subs);
   }
 }
 

@@ -91,10 +91,11 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out);
 int dd_set_weights(dd_handle* h, const dd_weights* w);
 
 /* How dd_rollout / dd_draft_block run the rollout after the z projection:
- * 0 (default) one persistent cooperative kernel for all prefix and draft
- * steps when the handle allows it (unsharded, at most 64 phases), else one
- * kernel per phase; 1 always one kernel per phase.  DD_ROLLOUT_PHASED=1 in
- * the environment selects 1 at dd_create.  Both give identical tokens. */
+ * 0 one persistent cooperative kernel for all prefix and draft steps when the
+ * handle allows it (unsharded, at most 64 phases), else one kernel per phase;
+ * 1 (default) always one kernel per phase, measured 1-5 % faster on B200.
+ * DD_ROLLOUT_PERSISTENT=1 in the environment selects 0 at dd_create.  Both
+ * give identical tokens. */
 int dd_set_rollout_mode(dd_handle* h, int mode);
 
 /* packed = 0 (default: stream the caller's row-major weights in place, no

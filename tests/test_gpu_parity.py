@@ -157,6 +157,7 @@ def test_persistent_rollout_matches_phased_exactly(B, H, G, E, V, S, P):
     rp = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
     rk = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
     lib = _lib.load()
+    assert lib.dd_set_rollout_mode(rp._h, 0) == _lib.DD_OK
     assert lib.dd_set_rollout_mode(rk._h, 1) == _lib.DD_OK
     for seed in range(2):
         prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=seed)
