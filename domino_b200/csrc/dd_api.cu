@@ -249,16 +249,15 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   }
   if (tiles > h->max_tiles) return fail(h, DD_EINVAL, "phase has %d tiles > %d", tiles, h->max_tiles);
   p.units = (long long)tiles * p.KC;
-  const int ctas = h->num_sms * (cls == PhaseClass::Big ? h->ctas_per_sm_big : h->ctas_per_sm_small);
-  int grid = (int)std::min<long long>(ctas, allow_split ? p.units : tiles);
-  if (grid < 1) grid = 1;
   p.b_bytes = (uint32_t)p.N * 128u;
   p.stage_bytes = kATileBytes + p.b_bytes;
   const uint32_t ring_budget =
       p.N > 64 ? 196u * 1024u : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
   p.stages = std::max(4, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
-  if ((size_t)p.stages * p.stage_bytes + 1024 + kSmemTail > 227 * 1024) p.stages = (227 * 1024 - 1024 - kSmemTail) / p.stage_bytes;
-  p.acc_slots = p.N <= 128 ? 2 : 1;
+  p.xpose_bytes = (kPhase == PH_ZLM || kPhase == PH_Z || kPhase == PH_TABLE) ? kXposeBytes : 0u;
+  const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes;
+  if ((size_t)p.stages * p.stage_bytes + fixed > 227 * 1024) p.stages = (227 * 1024 - fixed) / p.stage_bytes;
+  p.acc_slots = 2;  // the epilogue of one tile overlaps the next tile's MMAs (2 x 256 columns at most)
   // Up to four accumulators per slot within the per-CTA TMEM budget, so that
   // co-resident CTAs (2 per SM plus the next phase's) never wait for TMEM.
   p.nacc = 1;
@@ -270,11 +269,17 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   p.partials = h->partials;
   p.tile_counters = h->counters;
   p.status = h->status;
-  size_t smem = 1024 + (size_t)p.stages * p.stage_bytes + kSmemTail;
+  size_t smem = (size_t)p.stages * p.stage_bytes + fixed;
   // Big phases reserve enough shared memory that two CTAs of the same phase
   // never share an SM, while one small-phase CTA still fits beside them.
   if (cls == PhaseClass::Big && smem < (size_t)h->min_smem_kb_big * 1024) smem = (size_t)h->min_smem_kb_big * 1024;
   if (smem > 227 * 1024) return fail(h, DD_EINVAL, "shared memory %zu exceeds 227 KB", smem);
+  // One wave: no more CTAs than fit on the SMs at once (the stream-K split
+  // gives each the same work; a second wave would only add a tail).
+  const int fit = (int)(228u * 1024u / (uint32_t)(smem + 1024));
+  const int per_sm = std::max(1, std::min(fit, cls == PhaseClass::Big ? h->ctas_per_sm_big : h->ctas_per_sm_small));
+  int grid = (int)std::min<long long>((long long)h->num_sms * per_sm, allow_split ? p.units : tiles);
+  if (grid < 1) grid = 1;
   int rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
   rc = timing_begin(h, kPhase, st);

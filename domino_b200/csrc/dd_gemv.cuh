@@ -57,6 +57,10 @@ constexpr uint32_t kATileBytes = kTileM * 128;  // 16 KB
 constexpr int kMaxStages = 16;
 constexpr int kMaxBatch = 32;
 constexpr uint32_t kSmemTail = 2048;            // barriers + flags + argmax reduction
+// Staging area after the tail in phases whose epilogue writes X-row-major
+// outputs (z, base logits, the W_ih table): one 16-column chunk of a tile,
+// 16 x 128 elements of at most 4 bytes.
+constexpr uint32_t kXposeBytes = 16 * 128 * 4;
 
 constexpr int kMaxRanks = 8;
 
@@ -112,6 +116,7 @@ struct GemvParams {
   uint32_t stage_bytes;
   uint32_t b_bytes;
   int acc_slots;
+  uint32_t xpose_bytes;  // > 0: a kXposeBytes staging area follows the tail
   int nacc;          // independent accumulators per slot; K-step i goes to accumulator i % nacc
   uint32_t tmem_cols;
   uint32_t idesc;
@@ -218,7 +223,19 @@ struct AccView {
   long long U;
   int G, KC;
   uint32_t bar;        // named barrier of the 128 epilogue threads
+  void* xpose;         // shared staging chunk for row-contiguous stores, or null
+  long long row0;      // global row of the tile's first row
+  long long row_end;   // end of the segment's rows (exclusive, global)
 };
+
+// Four consecutive elements (8 or 16 bytes, aligned) from shared to global memory.
+template <typename T>
+__device__ __forceinline__ void store4(T* dst, const T* src) {
+  if constexpr (sizeof(T) == 2)
+    *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+  else
+    *reinterpret_cast<float4*>(dst) = *reinterpret_cast<const float4*>(src);
+}
 
 // This CTA's part of 16 accumulator columns [ch*16, ch*16+16): the sum of the
 // slot's accumulators in a fixed order.
@@ -289,24 +306,39 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
       if (kind == EPI_ZPROJ && p.fc1_bias) bias = IO::load((const T*)p.fc1_bias + row);
       if (kind == EPI_TABLE && p.b_ih) bias = IO::load((const T*)p.b_ih + row);
     }
+    T* out;
+    long long ld;
+    if (kind == EPI_LMHEAD) {
+      out = (T*)p.base_out;
+      ld = p.base_out_ld;
+    } else if (kind == EPI_ZPROJ) {
+      out = (T*)p.z_out;
+      ld = p.E;
+    } else {
+      out = (T*)p.table_out;
+      ld = p.table_ld;
+    }
+    // Column n of the output is row-contiguous: the tile's 128 rows are
+    // adjacent in memory, one X row apart from the next column.  Staged
+    // through shared memory, each warp store covers 128 rows of one column
+    // (4 elements per lane) instead of one element per lane, and a tile
+    // touches each column's page once instead of four times.
+    const bool xp = a.xpose != nullptr && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & (4 * sizeof(T) - 1)) == 0;
+    T* S = reinterpret_cast<T*>(a.xpose);
+    const int w4 = ept >> 5;
     for (int ch = 0; ch < nchunks; ++ch) {
       float v[16];
       acc_chunk(a, ch, v);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         const int n = ch * 16 + j;
-        if (n >= p.n_valid) break;
         const long long gn = (long long)p.n_off + n;
         const T val = IO::from_f(v[j] + bias);
-        if (valid) {
-          if (kind == EPI_LMHEAD)
-            ((T*)p.base_out)[gn * p.base_out_ld + row] = val;
-          else if (kind == EPI_ZPROJ)
-            ((T*)p.z_out)[gn * p.E + row] = val;
-          else
-            ((T*)p.table_out)[gn * p.table_ld + row] = val;
-        }
-        if (kind == EPI_LMHEAD && p.npre > 0) {
+        if (xp)
+          S[j * kTileM + a.r] = val;
+        else if (valid && n < p.n_valid)
+          out[gn * ld + row] = val;
+        if (kind == EPI_LMHEAD && p.npre > 0 && n < p.n_valid) {
           const int pos = (int)(gn % p.kpos);
           if (pos < p.npre) {  // uniform across the warp
             const float fv = IO::to_f(val);
@@ -315,6 +347,26 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
             if (lane == 0 && key) atomicMax(p.slots + (gn / p.kpos) * p.nslots + pos, key);
           }
         }
+      }
+      if (xp) {
+        named_bar_sync(a.bar, 128);
+        const long long r0 = a.row0 + 4 * lane;  // first of this lane's four rows
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = w4 + 4 * jj;
+          const int n = ch * 16 + j;
+          if (n < p.n_valid) {
+            T* dst = out + ((long long)p.n_off + n) * ld + r0;
+            const T* src = S + j * kTileM + 4 * lane;
+            if (r0 + 3 < a.row_end) {
+              store4<T>(dst, src);
+            } else {
+              for (int i = 0; i < 4; ++i)
+                if (r0 + i < a.row_end) dst[i] = src[i];
+            }
+          }
+        }
+        named_bar_sync(a.bar, 128);
       }
     }
     return;
@@ -729,6 +781,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N * p.nacc);
       a.nacc = p.nacc;
       a.bar = 1;
+      a.xpose = p.xpose_bytes ? tail + kSmemTail : nullptr;
+      a.row0 = row - r;
+      a.row_end = (long long)sg.row_off + sg.rows;
       a.combine = false;
       a.nseg = 1;
       a.myseg = 0;

@@ -416,6 +416,9 @@ __global__ void __launch_bounds__(2 * kThreads, 1)
           a.G = G;
           a.KC = KC;
           a.bar = ebar;
+          a.xpose = nullptr;  // no X-row-major outputs in the rollout phases
+          a.row0 = row - r;
+          a.row_end = (long long)sg.row_off + sg.rows;
           bool finish = true;
           if (kc0 > 0 || kc1 < KC) {
             const int c_lo = cta_of_unit(tile * KC, U, G);
