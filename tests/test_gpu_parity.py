@@ -182,9 +182,14 @@ def test_persistent_rollout_matches_phased_exactly(B, H, G, E, V, S, P):
     assert 9 in list(kinds[:n]), list(kinds[:n])
 
 
-def test_draft_block_fused_lm_head():
-    B, H, G, E, V, S, P = 3, 128, 128, 192, 1500, 13, 3
-    draft, target = random_modules(H, G, E, V, seed=31, fc2_std=0.08)
+@pytest.mark.parametrize("B,V", [
+    (3, 1500),   # one z / lm_head pass, N = 48
+    (20, 2048),  # B*K = 300 rows: two passes (256 + 44), staged row-contiguous stores
+    (20, 1501),  # same, base logits row stride not a multiple of 4: element-wise stores
+])
+def test_draft_block_fused_lm_head(B, V):
+    H, G, E, S, P = 128, 128, 192, 13, 3
+    draft, target = random_modules(H, G, E, V, seed=31 + B, fc2_std=0.08)
     r = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
     K = P - 1 + S
     g = torch.Generator().manual_seed(9)
