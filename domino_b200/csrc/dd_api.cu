@@ -120,6 +120,7 @@ struct dd_handle {
   // (default: measured faster on B200).
   unsigned int* rbar = nullptr;
   int rollout_mode = 1;
+  int min_units_per_cta = 8;
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
@@ -278,7 +279,11 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   // gives each the same work; a second wave would only add a tail).
   const int fit = (int)(228u * 1024u / (uint32_t)(smem + 1024));
   const int per_sm = std::max(1, std::min(fit, cls == PhaseClass::Big ? h->ctas_per_sm_big : h->ctas_per_sm_small));
-  int grid = (int)std::min<long long>((long long)h->num_sms * per_sm, allow_split ? p.units : tiles);
+  // At least min_units_per_cta units per CTA: a tile split over more CTAs
+  // costs its finisher one partial per CTA to add, more than the stream time
+  // the extra CTAs would save.
+  int grid = (int)std::min<long long>((long long)h->num_sms * per_sm,
+                                      allow_split ? std::max<long long>(1, p.units / h->min_units_per_cta) : tiles);
   if (grid < 1) grid = 1;
   int rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
@@ -848,6 +853,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
   h->pack = env_int("DD_PACK_WEIGHTS", 0, 0, 1) != 0;
   h->rollout_mode = env_int("DD_ROLLOUT_PERSISTENT", 0, 0, 1) ? 0 : 1;
+  h->min_units_per_cta = env_int("DD_MIN_UNITS_PER_CTA", h->min_units_per_cta, 1, 64);
   h->max_nacc = env_int("DD_NACC", h->max_nacc, 1, 4);
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", h->tmem_cols_per_cta, 32, 512);
   int prev = 0;
@@ -1342,6 +1348,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
     h.min_smem_kb_big = env_int("DD_MIN_SMEM_KB_BIG", defaults_source.min_smem_kb_big, 0, 227);
     h.ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", defaults_source.ctas_per_sm_big, 1, 2);
     h.ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", defaults_source.ctas_per_sm_small, 1, 2);
+    h.min_units_per_cta = env_int("DD_MIN_UNITS_PER_CTA", defaults_source.min_units_per_cta, 1, 64);
   }
   h.max_ctas = h.num_sms * std::max(h.ctas_per_sm_big, h.ctas_per_sm_small);
   // Widest accumulator any split tile of a rollout can have.
