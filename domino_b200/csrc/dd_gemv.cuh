@@ -294,6 +294,56 @@ __device__ __forceinline__ constexpr bool phase_has(int kind) {
   return false;
 }
 
+// Pure-draft prefix tokens: the argmax over the vocab of the base logits at
+// positions < npre, one 64-bit (value, index) word per row and position.  Out
+// of line: it runs only for blocks with a pure-draft prefix.
+template <typename T>
+__device__ __noinline__ void prefix_argmax_chunk(unsigned long long* slots, int nslots, long long gn0, int nv, int kpos,
+                                                 int npre, const T (&vals)[16], bool valid, uint32_t vocab_row,
+                                                 int lane) {
+  using IO = io<T>;
+  for (int j = 0; j < 16 && j < nv; ++j) {
+    const long long gn = gn0 + j;
+    const int pos = (int)(gn % kpos);
+    if (pos < npre) {  // uniform across the warp
+      const float fv = IO::to_f(vals[j]);
+      unsigned long long key = (valid && !isnan(fv)) ? argmax_key(fv, vocab_row) : 0ull;
+      key = warp_max_u64(key);
+      if (lane == 0 && key) atomicMax(slots + (gn / kpos) * nslots + pos, key);
+    }
+  }
+}
+
+// Row stride of the staging area, in elements: 2-byte columns are padded by
+// 64 bytes so that two consecutive columns start in opposite halves of the
+// shared-memory banks.
+template <typename T>
+constexpr int kXStride = sizeof(T) == 2 ? kTileM + 32 : kTileM;
+
+// Stage this thread's 16 column values of tile row r: S[j * kXStride + r].
+// 2-byte values go as 32-bit words of two rows: lane pairs swap one value
+// (even lanes write column j, odd lanes column j + 1), so each store covers
+// 16 words of two padded columns without bank conflicts.
+template <typename T>
+__device__ __forceinline__ void stage_columns(T* S, const T (&vals)[16], int r) {
+  if constexpr (sizeof(T) == 2) {
+    const bool odd = (r & 1) != 0;
+    uint32_t* S32 = reinterpret_cast<uint32_t*>(S);
+#pragma unroll
+    for (int j = 0; j < 16; j += 2) {
+      const uint32_t mine0 = *reinterpret_cast<const uint16_t*>(&vals[j]);
+      const uint32_t mine1 = *reinterpret_cast<const uint16_t*>(&vals[j + 1]);
+      const uint32_t got = __shfl_xor_sync(0xFFFFFFFFu, odd ? mine0 : mine1, 1);
+      const uint32_t word = odd ? (got | (mine1 << 16)) : (mine0 | (got << 16));
+      const int col = odd ? j + 1 : j;
+      S32[(col * kXStride<T> + (r & ~1)) >> 1] = word;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) S[j * kXStride<T> + r] = vals[j];
+  }
+}
+
 template <typename T, int kPhase>
 __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView& a, int kind, int row, bool valid,
                                               int q, int lane, unsigned long long* red, int ept) {
@@ -329,25 +379,19 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     for (int ch = 0; ch < nchunks; ++ch) {
       float v[16];
       acc_chunk(a, ch, v);
+      T vals[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const int n = ch * 16 + j;
-        const long long gn = (long long)p.n_off + n;
-        const T val = IO::from_f(v[j] + bias);
-        if (xp)
-          S[j * kTileM + a.r] = val;
-        else if (valid && n < p.n_valid)
-          out[gn * ld + row] = val;
-        if (kind == EPI_LMHEAD && p.npre > 0 && n < p.n_valid) {
-          const int pos = (int)(gn % p.kpos);
-          if (pos < p.npre) {  // uniform across the warp
-            const float fv = IO::to_f(val);
-            unsigned long long key = (valid && !isnan(fv)) ? argmax_key(fv, (uint32_t)(p.v_off + row)) : 0ull;
-            key = warp_max_u64(key);
-            if (lane == 0 && key) atomicMax(p.slots + (gn / p.kpos) * p.nslots + pos, key);
-          }
-        }
+      for (int j = 0; j < 16; ++j) vals[j] = IO::from_f(v[j] + bias);
+      if (xp) {
+        stage_columns<T>(S, vals, a.r);
+      } else if (valid) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (ch * 16 + j < p.n_valid) out[((long long)p.n_off + ch * 16 + j) * ld + row] = vals[j];
       }
+      if (kind == EPI_LMHEAD && p.npre > 0)
+        prefix_argmax_chunk<T>(p.slots, p.nslots, (long long)p.n_off + ch * 16, p.n_valid - ch * 16, p.kpos, p.npre,
+                               vals, valid, (uint32_t)(p.v_off + row), lane);
       if (xp) {
         named_bar_sync(a.bar, 128);
         const long long r0 = a.row0 + 4 * lane;  // first of this lane's four rows
@@ -357,7 +401,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           const int n = ch * 16 + j;
           if (n < p.n_valid) {
             T* dst = out + ((long long)p.n_off + n) * ld + r0;
-            const T* src = S + j * kTileM + 4 * lane;
+            const T* src = S + j * kXStride<T> + 4 * lane;
             if (r0 + 3 < a.row_end) {
               store4<T>(dst, src);
             } else {
