@@ -463,20 +463,20 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     return;
   }
   if (phase_has<kPhase>(EPI_FC2_ARGMAX) && kind == EPI_FC2_ARGMAX) {
-    float vals[64];
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch)
-      if (ch < nchunks) acc_chunk(a, ch, vals + ch * 16);
     const float bias = (valid && p.fc2_bias) ? IO::load((const T*)p.fc2_bias + row) : 0.0f;
-    // Groups of 8 batch rows: their base-logit loads are issued together,
-    // then the 8 independent warp reductions run.
+    if (p.B > 4) {
+      // One key per batch row in every lane, then a transposing butterfly:
+      // each round halves the keys a lane holds, so 31 shuffles leave lane l
+      // with the warp's maximum for batch row l (instead of 5 per row).
+      unsigned long long k[kMaxBatch];
 #pragma unroll
-    for (int b0 = 0; b0 < kMaxBatch; b0 += 8) {
-      if (b0 < p.B) {
+      for (int ch = 0; ch < kMaxBatch / 8; ++ch) {  // a 16-column chunk holds 8 rows (hi, lo)
+        float v[16];
+        if (ch < nchunks) acc_chunk(a, ch, v);
         float basev[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int b = b0 + i;
+          const int b = ch * 8 + i;
           basev[i] = 0.0f;
           if (b < p.B && valid) {
             const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
@@ -485,18 +485,43 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int b = b0 + i;
-          if (b < p.B) {
-            unsigned long long key = 0ull;
-            if (valid) {
-              float logit = vals[2 * b] + vals[2 * b + 1];
-              logit += bias;
-              logit += basev[i];
-              if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
-            }
-            key = warp_max_u64(key);
-            if (lane == 0) red[q * kMaxBatch + b] = key;
+          const int b = ch * 8 + i;
+          unsigned long long key = 0ull;
+          if (b < p.B && valid && ch < nchunks) {
+            const float logit = v[2 * i] + v[2 * i + 1] + bias + basev[i];
+            if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
           }
+          k[b] = key;
+        }
+      }
+#pragma unroll
+      for (int o = kMaxBatch / 2; o >= 1; o >>= 1) {
+        const bool up = (lane & o) != 0;
+#pragma unroll
+        for (int i = 0; i < o; ++i) {
+          const unsigned long long send = up ? k[i] : k[i + o];
+          const unsigned long long keep = up ? k[i + o] : k[i];
+          const unsigned long long got = __shfl_xor_sync(0xFFFFFFFFu, send, o);
+          k[i] = got > keep ? got : keep;
+        }
+      }
+      red[q * kMaxBatch + lane] = k[0];
+    } else {
+      float v[16];
+      acc_chunk(a, 0, v);  // 2B <= 8 columns
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        if (b < p.B) {
+          unsigned long long key = 0ull;
+          if (valid) {
+            const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
+            float logit = v[2 * b] + v[2 * b + 1];
+            logit += bias;
+            logit += IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+            if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
+          }
+          key = warp_max_u64(key);
+          if (lane == 0) red[q * kMaxBatch + b] = key;
         }
       }
     }
