@@ -166,9 +166,9 @@ int dd_accept(const int64_t* verify_ids, const int64_t* posterior, int32_t batch
  * replicates the rest; per draft step every rank computes its (logit, index)
  * argmax word and the fc2 kernel that finishes it writes it straight into
  * every rank's exchange buffer over NVLink (peer stores), after which the
- * next kernel on each rank takes the maximum over ranks.  This is the
- * all-reduce(max) on packed (logit, index) words that BASELINE.json's
- * north star describes, fused into the kernels (no separate collective).
+ * next kernel on each rank takes the maximum over ranks: an all-reduce(max)
+ * of packed (logit, index) words, fused into the kernels (no separate
+ * collective).
  * The s / gh projections (W_s, W_hh) are split by 128-row slices too: each
  * rank computes its slice, raises a flag in every rank's buffer, and a small
  * gather kernel copies the other ranks' slices in over NVLink.
