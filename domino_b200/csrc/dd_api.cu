@@ -282,8 +282,12 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   // At least min_units_per_cta units per CTA: a tile split over more CTAs
   // costs its finisher one partial per CTA to add, more than the stream time
   // the extra CTAs would save.
-  int grid = (int)std::min<long long>((long long)h->num_sms * per_sm,
-                                      allow_split ? std::max<long long>(1, p.units / h->min_units_per_cta) : tiles);
+  const long long slots = (long long)h->num_sms * per_sm;
+  int grid = (int)std::min<long long>(slots, allow_split ? std::max<long long>(1, p.units / h->min_units_per_cta) : tiles);
+  // Between half and all of the slots in tiles: one whole tile per CTA.  No
+  // tile is split, so no CTA waits to add partials at the end, which costs
+  // more than the unused slots save (s / gh at E = 12288: 192 tiles).
+  if (allow_split && tiles <= slots && 2LL * tiles >= slots) grid = tiles;
   if (grid < 1) grid = 1;
   int rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
