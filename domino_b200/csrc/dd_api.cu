@@ -284,10 +284,12 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   // the extra CTAs would save.
   const long long slots = (long long)h->num_sms * per_sm;
   int grid = (int)std::min<long long>(slots, allow_split ? std::max<long long>(1, p.units / h->min_units_per_cta) : tiles);
-  // Between half and all of the slots in tiles: one whole tile per CTA.  No
-  // tile is split, so no CTA waits to add partials at the end, which costs
-  // more than the unused slots save (s / gh at E = 12288: 192 tiles).
-  if (allow_split && tiles <= slots && 2LL * tiles >= slots) grid = tiles;
+  // Weight streams (N <= 64) with between half and all of the slots in
+  // tiles: one whole tile per CTA.  No tile is split, so no CTA waits to add
+  // partials at the end, which costs more than the unused slots save (s / gh
+  // at E = 12288: 192 tiles).  Wider passes are closer to tensor-bound and
+  // keep every SM.
+  if (allow_split && p.N <= 64 && tiles <= slots && 2LL * tiles >= slots) grid = tiles;
   if (grid < 1) grid = 1;
   int rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
