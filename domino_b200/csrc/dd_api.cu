@@ -284,12 +284,17 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   // the extra CTAs would save.
   const long long slots = (long long)h->num_sms * per_sm;
   int grid = (int)std::min<long long>(slots, allow_split ? std::max<long long>(1, p.units / h->min_units_per_cta) : tiles);
-  // Weight streams (N <= 64) with between half and all of the slots in
-  // tiles: one whole tile per CTA.  No tile is split, so no CTA waits to add
-  // partials at the end, which costs more than the unused slots save (s / gh
-  // at E = 12288: 192 tiles).  Wider passes are closer to tensor-bound and
-  // keep every SM.
-  if (allow_split && p.N <= 64 && tiles <= slots && 2LL * tiles >= slots) grid = tiles;
+  // Weight streams (N <= 64) with no more tiles than slots: every tile is cut
+  // into the same number k <= 4 of CTA ranges (k = 1: one whole tile per CTA),
+  // as long as that uses at least half the slots.  A finisher then adds at
+  // most k - 1 partials, where a stream-K cut over all slots can leave it a
+  // longer chain than the extra slots save (s / gh at E = 12288: 192 tiles,
+  // k = 1; at E = 1024: 104 tiles, k = 2).  Wider passes are closer to
+  // tensor-bound and keep every SM.
+  if (allow_split && p.N <= 64 && tiles <= slots) {
+    const long long k = std::min<long long>(4, slots / tiles);
+    if (2LL * tiles * k >= slots) grid = (int)(tiles * k);
+  }
   if (grid < 1) grid = 1;
   int rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
