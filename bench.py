@@ -19,8 +19,12 @@ Multi-GPU: one process per GPU, each runs its own batch (requests are
 independent; no collective on the data path): weak scaling.  Times are CUDA
 events on each rank, max over ranks.
 
-``--impl reference`` times the CPU oracle (a numpy restatement of the
-reference's draft step) on this host's cores on the same workload.
+``--impl reference`` times the reference's CPU path of the draft step on this
+host's cores, on the same workload, config, steps and warm-up: the op
+sequence of its PyTorch branch (code/kernel/domino.py:374-431) restated in
+oracle/torch_branch.py, whose tokens equal the reference's.  The reference
+itself is a Python source tree without packaging metadata (no setup.py or
+pyproject.toml), so it cannot be installed where this benchmark runs.
 """
 from __future__ import annotations
 
@@ -97,6 +101,17 @@ def fc2_bytes(B, E, V, w=2):
 def workload_name(args, B, H, G, E, V, S, P):
     return (f"{args.model}-shaped Domino draft head, bf16, batch {B}/GPU, block {args.block} "
             f"({S} draft + {P} prefix tokens), H={H} G={G} E={E} V={V}")
+
+
+def bench_config(args, B, rows_total, world, sharded, H, G, E, V, S, P):
+    """The ``config`` dict of the JSON line; both arms print the same one."""
+    return {
+        "workload": workload_name(args, B, H, G, E, V, S, P),
+        "batch_per_gpu": B, "global_batch": rows_total, "block": args.block, "seq_len": args.block,
+        "parallelism": (f"vocab{world} (fc2 / lm_head rows sharded; argmax words exchanged over NVLink "
+                        "inside the kernels)") if sharded else f"dp{world} (request batch sharded, no collective)",
+        "l2": "no flush: inputs larger than L2 (the weights streamed every step are ~70x the 126 MB L2)",
+    }
 
 
 def measured_peak_hbm():
@@ -387,13 +402,7 @@ def run_ours(args):
             "dtype": "bf16",
             "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1), "
                     "target tokens = draft tokens for the first k~U{0..15} positions",
-            "config": {
-                "workload": workload_name(args, B, H, G, E, V, S, P),
-                "batch_per_gpu": B, "global_batch": rows_total, "block": args.block, "seq_len": args.block,
-                "parallelism": (f"vocab{world} (fc2 / lm_head rows sharded; argmax words exchanged over NVLink "
-                                "inside the kernels)") if sharded else f"dp{world} (request batch sharded, no collective)",
-                "l2": "no flush: 8.7 GB of weights streamed per step, ~70x the 126 MB L2",
-            },
+            "config": bench_config(args, B, rows_total, world, sharded, H, G, E, V, S, P),
             "roofline": {
                 "bound": "hbm", "kernel": "fc2 phase (gemv_stream_kernel PH_FC2)",
                 "achieved": round(achieved, 1), "peak": peak, "peak_source": peak_src, "unit": "GB/s",
@@ -423,66 +432,63 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# ---------------------------------------------------------------- CPU oracle
-def oracle_setup(draft, target, P):
-    """fp32 host copies of the head weights for the numpy oracle."""
-    from oracle import draft_oracle as O
-
-    def f32(t):
-        return t.detach().float().cpu().numpy()
-
-    fc1 = draft.embed_proj[0].weight
-    w = O.DraftWeights(fc1=f32(fc1), fc2=f32(draft.embed_proj[2].weight), w_ih=f32(draft.prefix_gru.weight_ih_l0),
-                       w_hh=f32(draft.prefix_gru.weight_hh_l0), embed=None, dtype="bf16")
+# ---------------------------------------------------------------- CPU leg
+def cpu_head(draft, target):
+    """Host copies of the head for the CPU leg (oracle/torch_branch.py: the
+    reference's PyTorch-branch op sequence in torch CPU kernels).  The
+    one-time W_ih table is built where the modules live (the GPU) and copied."""
     import torch
-    tab = torch.nn.functional.linear(target.model.embed_tokens.weight, draft.prefix_gru.weight_ih_l0)
-    w.table = f32(tab)
-    del tab
-    return w, f32(target.lm_head.weight)
+    import torch.nn.functional as F
+
+    from oracle import torch_branch as TB
+
+    gru = draft.prefix_gru
+    with torch.inference_mode():
+        table = F.linear(target.model.embed_tokens.weight, gru.weight_ih_l0,
+                         gru.bias_ih_l0 if gru.bias else None).cpu()
+    return TB.head_from_modules(draft, target, table=table)
 
 
-def oracle_block(w, lm, ph, last, S, P):
-    """One block of the oracle: lm_head, pure-draft prefix, rollout."""
-    from oracle import draft_oracle as O
-    import numpy as np
+def cpu_block(head, ph, last, P):
+    """One block of the CPU leg: lm_head, pure-draft prefix, rollout (code/dflash.py:424-439)."""
+    from oracle import torch_branch as TB
 
-    base = O.lm_head(ph, lm, "bf16")
-    pre = O.pure_draft_prefix(base, P) if P else np.zeros((ph.shape[0], 0), np.int64)
-    prefix = np.concatenate([last.reshape(-1, 1), pre], 1)
-    tr = O.rollout(w, prefix, ph[:, P:], base[:, P:])
-    return tr.tokens
+    return TB.draft_block(head, last, ph, P)
 
 
 def cpu_baseline(args, draft, target, ph, last, budget_s):
-    """Time the oracle on this host's cores on blocks of the same workload."""
-    import numpy as np
+    """Time the CPU leg on this host's cores on blocks of the same workload."""
+    import torch
 
     H, G, E, V, S, P = shapes(args)
     threads = host_threads()
-    w, lm = oracle_setup(draft, target, P)
-    w.embed = np.zeros((1, H), np.float32)  # H is read from embed's shape; the table is given
-    ph_np = ph.float().cpu().numpy()
-    last_np = last.cpu().numpy()
+    head = cpu_head(draft, target)
+    ph_c, last_c = ph.cpu(), last.cpu()
+    cpu_block(head, ph_c, last_c, P)  # warm-up
     # A bounded sample: whole blocks until about a third of the budget (10 s of
     # the default 30 s) has passed, at least one block and at most 64.
     blocks, t0 = 0, time.perf_counter()
     while True:
-        oracle_block(w, lm, ph_np, last_np, S, P)
+        cpu_block(head, ph_c, last_c, P)
         blocks += 1
         if time.perf_counter() - t0 > budget_s / 3 or blocks >= 64:
             break
     dt = time.perf_counter() - t0
     return {
         "value": round(blocks * args.batch * S / dt, 4), "unit": "draft tokens/s", "cores": threads,
-        "kind": "port", "threads": "numpy BLAS, all host threads",
+        "kind": "port", "threads": f"torch CPU, {torch.get_num_threads()} threads",
         "sample": f"{blocks} full block(s) of the same workload (batch {args.batch}, {S} draft tokens each) "
-                  f"through oracle/draft_oracle.py in fp32 numpy, {dt:.1f} s",
+                  f"through oracle/torch_branch.py (the reference's PyTorch-branch op sequence, bf16 torch CPU "
+                  f"kernels), {dt:.1f} s",
     }
 
 
 def host_threads() -> int:
-    """Use every host thread for the oracle's BLAS calls (torchrun sets OMP_NUM_THREADS=1)."""
+    """Use every host thread for the CPU leg (torchrun sets OMP_NUM_THREADS=1)."""
+    import torch
+
     n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    torch.set_num_threads(n)
     try:
         from threadpoolctl import threadpool_limits
         threadpool_limits(n)
@@ -492,38 +498,51 @@ def host_threads() -> int:
 
 
 def run_reference(args):
+    """The reference arm: the reference's PyTorch-branch op sequence
+    (oracle/torch_branch.py) on this host's cores, on the same workload,
+    config, steps and warm-up as our arm at this N.  Rank 0 alone runs it; the
+    other ranks exit without work."""
     world, rank, local = dist_env()
     if rank != 0:
         return
     threads = host_threads()
-    import numpy as np
     import torch
+
+    from domino_b200.parallel import shard_rows
 
     H, G, E, V, S, P = shapes(args)
     B = args.batch
+    sharded = args.vocab_shard and world > 1
+    if args.global_batch is not None:
+        B = shard_rows(args.global_batch, world, 0)[1]
+        rows_total = args.global_batch
+    elif sharded:
+        rows_total = B
+    else:
+        rows_total = B * world
     K = S + P
     dev = torch.device("cuda", local) if torch.cuda.is_available() else torch.device("cpu")
     # Weights are generated on the GPU only for speed; everything timed runs on the host.
     draft, target = build_modules(H, G, E, V, dev, args.seed)
-    w, lm = oracle_setup(draft, target, P)
-    w.embed = np.zeros((1, H), np.float32)
+    head = cpu_head(draft, target)
     del draft, target
-    rng = np.random.default_rng(args.seed)
-    from oracle.draft_oracle import round_to
-    blocks = [(round_to(rng.standard_normal((B, K, H)).astype(np.float32), "bf16"),
-               rng.integers(0, V, (B,))) for _ in range(2)]
+    g = torch.Generator().manual_seed(args.seed)
+    blocks = [(torch.randn(rows_total, K, H, generator=g).to(torch.bfloat16),
+               torch.randint(0, V, (rows_total,), generator=g)) for _ in range(2)]
     t0 = time.perf_counter()
-    oracle_block(w, lm, blocks[0][0], blocks[0][1], S, P)
+    cpu_block(head, blocks[0][0], blocks[0][1], P)
     t_block = time.perf_counter() - t0
+    # A bounded sample: all requested steps unless they would take longer
+    # than the budget (then as many whole blocks as fit).
     n_steps = max(1, min(args.steps, int(args.cpu_budget_s / max(t_block, 1e-3))))
-    n_warm = min(args.warmup, 1)
+    n_warm = max(0, args.warmup - 1)  # the sizing block above was the first warm-up step
     for i in range(n_warm):
-        oracle_block(w, lm, *blocks[i % 2], S, P)
+        cpu_block(head, *blocks[i % 2], P)
     t0 = time.perf_counter()
     for i in range(n_steps):
-        oracle_block(w, lm, *blocks[i % 2], S, P)
+        cpu_block(head, *blocks[i % 2], P)
     dt = time.perf_counter() - t0
-    value = n_steps * B * S / dt
+    value = n_steps * rows_total * S / dt
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -531,19 +550,22 @@ def run_reference(args):
         "unit": "draft tokens/s",
         "n_gpus": world,
         "steps": n_steps,
-        "warmup": n_warm,
+        "warmup": args.warmup,
         "ms_per_step": round(dt / n_steps * 1e3, 2),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong" if (args.global_batch is not None or sharded) else "weak",
         "vs_baseline": None,
-        "dtype": "bf16 values in fp32 numpy",
-        "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1)",
-        "config": {"workload": workload_name(args, B, H, G, E, V, S, P), "batch_per_gpu": B,
-                   "global_batch": B, "block": args.block, "parallelism": "host CPU, rank 0 only"},
+        "dtype": "bf16",
+        "data": "synthetic: seeded random-init weights N(0,0.02), hidden states N(0,1), "
+                "target tokens = draft tokens for the first k~U{0..15} positions",
+        "config": bench_config(args, B, rows_total, world, sharded, H, G, E, V, S, P),
         "cpu_baseline": {"value": round(value, 4), "unit": "draft tokens/s", "cores": threads,
                          "kind": "port",
-                         "sample": f"{n_steps} block(s) of batch {B} (of {args.steps} requested; capped at "
-                                   f"~{args.cpu_budget_s:.0f} s), oracle/draft_oracle.py fp32 numpy, all host threads"},
+                         "sample": f"{n_steps} whole block(s) of all {rows_total} rows (of {args.steps} requested; "
+                                   f"capped at ~{args.cpu_budget_s:.0f} s) through oracle/torch_branch.py (the "
+                                   "reference's PyTorch-branch op sequence, code/kernel/domino.py:374-431, in bf16 "
+                                   "torch CPU kernels; its tokens equal the reference's), all host threads, rank 0 "
+                                   "only"},
         "e2e": {"value": round(value, 4), "unit": "draft tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }

@@ -28,9 +28,10 @@ DD_STATUS_NO_ARGMAX = 4
 EXPORTS = (
     "dd_create", "dd_set_weights", "dd_build_table", "dd_rollout", "dd_draft_block",
     "dd_accept", "dd_get_status", "dd_last_error", "dd_version", "dd_destroy",
-    "dd_set_timing", "dd_read_timing", "dd_rollout_noalloc",
+    "dd_set_timing", "dd_read_timing", "dd_rollout_noalloc", "dd_noalloc_status",
     "dd_get_exchange_buffer", "dd_ipc_export", "dd_ipc_open", "dd_ipc_close", "dd_set_vocab_shard",
     "dd_set_exchange_timeout", "dd_verify_accept", "dd_set_weight_layout", "dd_set_rollout_mode",
+    "dd_set_trace",
 )
 PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell", 8: "gather", 9: "rollout"}
 
@@ -61,6 +62,10 @@ class DDWeights(ctypes.Structure):
     ]
 
 
+class DDTrace(ctypes.Structure):
+    _fields_ = [("z", ctypes.c_void_p), ("h", ctypes.c_void_p), ("gh", ctypes.c_void_p), ("s", ctypes.c_void_p)]
+
+
 class DominoDraftError(RuntimeError):
     """A libdomino_draft call returned a negative status."""
 
@@ -89,6 +94,7 @@ def load() -> ctypes.CDLL:
         lib.dd_rollout.argtypes = [vp, vp, vp, vp, vp, vp]
         lib.dd_rollout_noalloc.argtypes = [ctypes.POINTER(DDConfig), ctypes.POINTER(DDWeights), ctypes.c_int,
                                            vp, vp, vp, vp, vp]
+        lib.dd_noalloc_status.argtypes = [ctypes.c_int]
         lib.dd_draft_block.argtypes = [vp, vp, vp, vp, vp, vp]
         lib.dd_accept.argtypes = [vp, vp, i32, i32, vp, vp, vp]
         lib.dd_get_status.argtypes = [vp]
@@ -107,6 +113,7 @@ def load() -> ctypes.CDLL:
         lib.dd_verify_accept.argtypes = [vp, vp, i32, i32, vp, vp, vp, vp, vp]
         lib.dd_set_weight_layout.argtypes = [vp, ctypes.c_int]
         lib.dd_set_rollout_mode.argtypes = [vp, ctypes.c_int]
+        lib.dd_set_trace.argtypes = [vp, ctypes.POINTER(DDTrace)]
         lib.dd_read_timing.argtypes = [vp, vp, vp, i32]
         for name in EXPORTS:
             if name not in ("dd_last_error", "dd_version"):

@@ -125,6 +125,9 @@ struct dd_handle {
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
   unsigned int* vdone = nullptr;
+  // Opt-in state trace (dd_set_trace): per-step copies of z, h, gh and s.
+  bool tracing = false;
+  dd_trace trace{};
   // Opt-in per-launch timing (dd_set_timing): an event pair around each launch.
   static constexpr int kMaxTimed = 4096;
   bool timing = false;
@@ -410,6 +413,15 @@ int launch_gather(dd_handle* h, int slot, bool with_gh, cudaStream_t st) {
   return timing_end(h, st);
 }
 
+// Trace copies (dd_set_trace): `rows` x `cols` elements of the weight dtype
+// from a scratch buffer into entry `idx` of a caller trace array.
+int trace_copy(dd_handle* h, void* dst, int idx, const void* src, long long rows, long long cols, cudaStream_t st) {
+  if (!h->tracing || !dst) return DD_OK;
+  const size_t bytes = (size_t)rows * cols * 2;
+  DD_CUDA(h, cudaMemcpyAsync(static_cast<uint8_t*>(dst) + (size_t)idx * bytes, src, bytes, cudaMemcpyDeviceToDevice, st));
+  return DD_OK;
+}
+
 // Z (+ lm_head) phase over the X = parallel_hiddens rows, in passes of <= 256 rows.
 template <typename T>
 int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* base_out, cudaStream_t st) {
@@ -450,7 +462,7 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
     }
     if (rc) return rc;
   }
-  return DD_OK;
+  return trace_copy(h, h->trace.z, 0, h->zbuf, rows, c.emb_dim, st);
 }
 
 // GRU prefix + S rollout steps.  Token sources: ids (runner) or the prefix
@@ -477,6 +489,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     cp.write_h = 1;
     cp.h_out = h->hbuf[0];
     rc = launch_cell<T>(h, cp, st);
+    if (!rc) rc = trace_copy(h, h->trace.h, 0, h->hbuf[0], c.batch, c.gru_hidden, st);
     if (rc) return rc;
   }
   const int n_prefix_total = n_prefix_ids + npre;  // GRU inputs before the rollout
@@ -491,6 +504,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     p.b_hh = h->w.b_hh;
     p.packed[0] = static_cast<const uint8_t*>(h->pk_whh);
     rc = launch_gemv<T, PH_GH>(h, h->tm_whh, nullptr, h->tm_h[cur], p, PhaseClass::Small, true, st);
+    if (!rc) rc = trace_copy(h, h->trace.gh, j - 1, h->ghbuf, c.batch, 3LL * c.gru_hidden, st);
     if (rc) return rc;
     CellParams cp;
     memset(&cp, 0, sizeof(cp));
@@ -513,6 +527,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     cp.h_in = h->hbuf[cur];
     cp.h_out = h->hbuf[cur ^ 1];
     rc = launch_cell<T>(h, cp, st);
+    if (!rc) rc = trace_copy(h, h->trace.h, j, h->hbuf[cur ^ 1], c.batch, c.gru_hidden, st);
     if (rc) return rc;
     cur ^= 1;
   }
@@ -539,9 +554,12 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.mid_out = h->midbuf;
       p.gh_out = h->ghbuf;
       p.b_hh = h->w.b_hh;
+      if (h->tracing && h->trace.s) p.s_out = static_cast<uint8_t*>(h->trace.s) + (size_t)t * c.batch * c.emb_dim * 2;
       p.packed[0] = static_cast<const uint8_t*>(h->pk_ws);
       p.packed[1] = static_cast<const uint8_t*>(h->pk_whh);
       rc = launch_gemv<T, PH_SGH>(h, h->tm_ws, last ? nullptr : &h->tm_whh, h->tm_h[cur], p, PhaseClass::Small, true, st);
+      if (!rc && !last)
+        rc = trace_copy(h, h->trace.gh, n_prefix_total - 1 + t, h->ghbuf, c.batch, 3LL * c.gru_hidden, st);
       if (rc) return rc;
       if (h->sgh_sharded) {
         rc = launch_gather(h, npre + t, !last, st);
@@ -584,6 +602,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       cp.h_in = h->hbuf[cur];
       cp.h_out = h->hbuf[cur ^ 1];
       rc = launch_cell<T>(h, cp, st);
+      if (!rc && !last) rc = trace_copy(h, h->trace.h, n_prefix_total + t, h->hbuf[cur ^ 1], c.batch, c.gru_hidden, st);
       if (rc) return rc;
       cur ^= 1;
     }
@@ -603,7 +622,7 @@ int run_rollout_persistent(dd_handle* h, const int64_t* ids, int ids_ld, int n_p
   const dd_config& c = h->cfg;
   const int n_prefix_total = n_prefix_ids + npre;
   const int nphases = 1 + 2 * (n_prefix_total - 1) + 3 * c.steps;
-  if (h->rollout_mode != 0 || h->world > 1 || nphases > kMaxRollPhases) return DD_EUNSUPPORTED;
+  if (h->rollout_mode != 0 || h->world > 1 || h->tracing || nphases > kMaxRollPhases) return DD_EUNSUPPORTED;
   static RollParams rp;  // ~10 KB: kept off the stack; the handle is not thread-safe anyway
   memset(&rp, 0, sizeof(rp));
   GemvParams& gp = rp.gp;
@@ -801,6 +820,31 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
   return DD_OK;
 }
 
+// Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
+// DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
+// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS) over the defaults of a fresh
+// handle.  dd_create and dd_rollout_noalloc both read them here, so the two
+// entry points always build the same launches.
+void read_launch_env(dd_handle* h) {
+  auto env_int = [](const char* name, int def, int lo, int hi) {
+    const char* v = getenv(name);
+    if (!v || !*v) return def;
+    const int x = atoi(v);
+    return x < lo ? lo : (x > hi ? hi : x);
+  };
+  const dd_handle d{};
+  h->ring_kb_big = env_int("DD_RING_KB_BIG", d.ring_kb_big, 36, 220);
+  h->ring_kb_small = env_int("DD_RING_KB_SMALL", d.ring_kb_small, 36, 220);
+  h->min_smem_kb_big = env_int("DD_MIN_SMEM_KB_BIG", d.min_smem_kb_big, 0, 227);
+  h->ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", d.ctas_per_sm_big, 1, 2);
+  h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", d.ctas_per_sm_small, 1, 2);
+  h->pack = env_int("DD_PACK_WEIGHTS", 0, 0, 1) != 0;
+  h->rollout_mode = env_int("DD_ROLLOUT_PERSISTENT", 0, 0, 1) ? 0 : 1;
+  h->min_units_per_cta = env_int("DD_MIN_UNITS_PER_CTA", d.min_units_per_cta, 1, 64);
+  h->max_nacc = env_int("DD_NACC", d.max_nacc, 1, 4);
+  h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", d.tmem_cols_per_cta, 32, 512);
+}
+
 }  // namespace
 
 // ============================================================================ C ABI
@@ -850,23 +894,8 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
     h->xbuf_bytes = bytes;
   }
   h->max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
-  auto env_int = [](const char* name, int def, int lo, int hi) {
-    const char* v = getenv(name);
-    if (!v || !*v) return def;
-    const int x = atoi(v);
-    return x < lo ? lo : (x > hi ? hi : x);
-  };
-  h->ring_kb_big = env_int("DD_RING_KB_BIG", h->ring_kb_big, 36, 220);
-  h->ring_kb_small = env_int("DD_RING_KB_SMALL", h->ring_kb_small, 36, 220);
-  h->min_smem_kb_big = env_int("DD_MIN_SMEM_KB_BIG", h->min_smem_kb_big, 0, 227);
-  h->ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", h->ctas_per_sm_big, 1, 2);
-  h->ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", h->ctas_per_sm_small, 1, 2);
+  read_launch_env(h);
   h->max_ctas = h->num_sms * std::max(h->ctas_per_sm_big, h->ctas_per_sm_small);
-  h->pack = env_int("DD_PACK_WEIGHTS", 0, 0, 1) != 0;
-  h->rollout_mode = env_int("DD_ROLLOUT_PERSISTENT", 0, 0, 1) ? 0 : 1;
-  h->min_units_per_cta = env_int("DD_MIN_UNITS_PER_CTA", h->min_units_per_cta, 1, 64);
-  h->max_nacc = env_int("DD_NACC", h->max_nacc, 1, 4);
-  h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", h->tmem_cols_per_cta, 32, 512);
   int prev = 0;
   cudaGetDevice(&prev);
   auto cleanup_fail = [&](int code) {
@@ -1196,6 +1225,14 @@ int dd_set_exchange_timeout(dd_handle* h, uint64_t timeout_ns) {
   return DD_OK;
 }
 
+int dd_set_trace(dd_handle* h, const dd_trace* t) {
+  if (!h) return DD_EINVAL;
+  if (t && h->world > 1) return fail(h, DD_EINVAL, "dd_set_trace: vocab-sharded handles hold only slices of s and gh");
+  h->tracing = t != nullptr;
+  h->trace = t ? *t : dd_trace{};
+  return DD_OK;
+}
+
 int dd_set_timing(dd_handle* h, int enable) {
   if (!h) return DD_EINVAL;
   h->timing = enable != 0;
@@ -1268,6 +1305,7 @@ int dd_destroy(dd_handle* h) {
 namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(32) << 20;  // 32 MiB
 constexpr int kNoAllocMaxDevices = 16;
+constexpr size_t kNoAllocStatusBytes = 256;  // the status word, at offset 0
 }  // namespace
 
 // One copy per device that loads this library's kernels, held until exit.
@@ -1333,44 +1371,34 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.cfg = c;
   h.have_weights = false;
   h.timing = false;
+  h.tracing = false;
   h.n_timed = 0;
   h.err[0] = 0;
   h.N1 = round_up(c.batch, 16);
   h.N2 = round_up(2 * c.batch, 16);
-  h.pack = false;  // packing would allocate: stream the caller's row-major weights
   h.v_off = 0;
   h.v_local = c.vocab;  // unsharded
   h.world = 1;
   h.rank = 0;
-  h.rollout_mode = 1;  // one launch per phase: the persistent kernel's grid counters are not in this scratch
   const int npre_max = c.prefix_tokens - 1;
   h.nslots = npre_max + c.steps;
   h.max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
-  {
-    auto env_int = [](const char* name, int def, int lo, int hi) {
-      const char* v = getenv(name);
-      if (!v || !*v) return def;
-      const int x = atoi(v);
-      return x < lo ? lo : (x > hi ? hi : x);
-    };
-    const dd_handle defaults_source{};
-    h.ring_kb_big = env_int("DD_RING_KB_BIG", defaults_source.ring_kb_big, 36, 220);
-    h.ring_kb_small = env_int("DD_RING_KB_SMALL", defaults_source.ring_kb_small, 36, 220);
-    h.min_smem_kb_big = env_int("DD_MIN_SMEM_KB_BIG", defaults_source.min_smem_kb_big, 0, 227);
-    h.ctas_per_sm_big = env_int("DD_CTAS_PER_SM_BIG", defaults_source.ctas_per_sm_big, 1, 2);
-    h.ctas_per_sm_small = env_int("DD_CTAS_PER_SM_SMALL", defaults_source.ctas_per_sm_small, 1, 2);
-    h.min_units_per_cta = env_int("DD_MIN_UNITS_PER_CTA", defaults_source.min_units_per_cta, 1, 64);
-  }
+  read_launch_env(&h);
+  h.pack = false;      // packing would allocate: stream the caller's row-major weights
+  h.rollout_mode = 1;  // one launch per phase: the persistent kernel's grid counters are not in this scratch
   h.max_ctas = h.num_sms * std::max(h.ctas_per_sm_big, h.ctas_per_sm_small);
   // Widest accumulator any split tile of a rollout can have.
   const int n_part = std::max(std::min(256, round_up(c.batch * c.steps, 16)), std::max(h.N1, h.N2));
   const size_t positions = (size_t)npre_max + c.steps;
-  size_t off = 0;
+  // The status word sits at a fixed place, the first 256 bytes, so that
+  // dd_noalloc_status can find it whatever the shapes of the last call.
+  size_t off = kNoAllocStatusBytes;
   auto take = [&](size_t bytes) {
     unsigned char* p = d.base + off;
     off = (off + bytes + 255) & ~size_t(255);
     return p;
   };
+  h.status = reinterpret_cast<unsigned int*>(d.base);
   h.zbuf = take((size_t)c.batch * positions * c.emb_dim * 2);
   h.midbuf = take((size_t)h.N2 * c.emb_dim * 2);
   h.hbuf[0] = take((size_t)h.N1 * c.gru_hidden * 2);
@@ -1379,7 +1407,6 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.slots = reinterpret_cast<unsigned long long*>(take((size_t)c.batch * h.nslots * 8));
   h.partials = reinterpret_cast<float*>(take((size_t)2 * h.max_ctas * n_part * kTileM * 4));
   h.counters = reinterpret_cast<unsigned int*>(take((size_t)h.max_tiles * 4));
-  h.status = reinterpret_cast<unsigned int*>(take(64));
   if (off > kNoAllocScratchBytes)
     return fail(nullptr, DD_EINVAL,
                 "dd_rollout_noalloc: these shapes need %zu bytes of scratch; the static scratch holds %zu "
@@ -1387,7 +1414,9 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
                 off, kNoAllocScratchBytes);
 
   // The scratch keeps the previous call's contents: clear what must start at
-  // zero (operand padding rows, split-tile counters, status).
+  // zero (operand padding rows, split-tile counters).  The status word is
+  // left alone: it collects the bits of every call until dd_noalloc_status
+  // reads and clears it.
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const struct {
     void* p;
@@ -1395,8 +1424,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   } zero[] = {{h.midbuf, (size_t)h.N2 * c.emb_dim * 2},
               {h.hbuf[0], (size_t)h.N1 * c.gru_hidden * 2},
               {h.hbuf[1], (size_t)h.N1 * c.gru_hidden * 2},
-              {h.counters, (size_t)h.max_tiles * 4},
-              {h.status, 64}};
+              {h.counters, (size_t)h.max_tiles * 4}};
   for (const auto& z : zero)
     if (cudaMemsetAsync(z.p, 0, z.n, st) != cudaSuccess)
       return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cudaMemsetAsync failed");
@@ -1407,4 +1435,22 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   if (!rc) rc = dd_set_weights(&h, w);
   if (!rc) rc = dd_rollout(&h, prefix_ids, parallel_hiddens, base_logits, out_tokens, stream);
   return rc ? noalloc_fail(&h, rc) : DD_OK;
+}
+
+extern "C" int dd_noalloc_status(int device) {
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return fail(nullptr, DD_EINVAL, "dd_noalloc_status: device %d outside [0, %d)", device, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  const NoAllocDevice& d = g_noalloc[device];
+  if (!d.ready) return 0;  // no allocation-free call has run on this device
+  int prev = 0;
+  cudaGetDevice(&prev);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(nullptr, DD_ECUDA, "dd_noalloc_status: cudaSetDevice failed");
+  unsigned int s = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(&s, d.base, sizeof(s), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemset(d.base, 0, sizeof(s));
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(nullptr, DD_ECUDA, "dd_noalloc_status: %s", cudaGetErrorString(e));
+  return (int)s;
 }

@@ -241,15 +241,19 @@ constexpr int kVerifyThreads = 256;
 constexpr int kVerifyChunk = 8192;
 
 template <typename L>
-__device__ __forceinline__ float logit_at(const L* p, size_t i);
+__device__ __forceinline__ float logit_f(L v);
 template <>
-__device__ __forceinline__ float logit_at<float>(const float* p, size_t i) { return p[i]; }
+__device__ __forceinline__ float logit_f<float>(float v) { return v; }
 template <>
-__device__ __forceinline__ float logit_at<__nv_bfloat16>(const __nv_bfloat16* p, size_t i) {
-  return __bfloat162float(p[i]);
+__device__ __forceinline__ float logit_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float logit_f<__half>(__half v) { return __half2float(v); }
+
+template <typename L>
+__device__ __forceinline__ unsigned long long max_key(unsigned long long best, L v, int idx) {
+  const unsigned long long k = argmax_key(logit_f<L>(v), (uint32_t)idx);
+  return k > best ? k : best;
 }
-template <>
-__device__ __forceinline__ float logit_at<__half>(const __half* p, size_t i) { return __half2float(p[i]); }
 
 template <typename L>
 __global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* logits, int V, int B, int K1,
@@ -265,14 +269,24 @@ __global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* 
   const int v0 = blockIdx.x * kVerifyChunk;
   const int v1 = min(V, v0 + kVerifyChunk);
   const L* src = logits + (size_t)row * V;
+  // 16-byte loads over the aligned middle of [v0, v1); rows of odd length
+  // start anywhere, so the first `head` elements and the tail go one by one.
+  constexpr int kVec = 16 / (int)sizeof(L);
+  const int head = min(v1 - v0, (int)(((16u - (reinterpret_cast<uintptr_t>(src + v0) & 15u)) & 15u) / sizeof(L)));
+  const int nvec = (v1 - v0 - head) / kVec;
+  const int vtail = v0 + head + nvec * kVec;
   unsigned long long best = 0ull;
-  for (int v = v0 + threadIdx.x; v < v1; v += kVerifyThreads) {
-    const float x = logit_at<L>(src, v);
-    if (!isnan(x)) {
-      const unsigned long long k = argmax_key(x, (uint32_t)v);
-      best = k > best ? k : best;
-    }
+  const uint4* vsrc = reinterpret_cast<const uint4*>(src + v0 + head);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < nvec; i += kVerifyThreads) {
+    const uint4 raw = __ldcs(vsrc + i);  // read once: do not keep it in L2
+    const L* e = reinterpret_cast<const L*>(&raw);
+    const int vb = v0 + head + i * kVec;
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) best = max_key<L>(best, e[j], vb + j);
   }
+  if ((int)threadIdx.x < head) best = max_key<L>(best, src[v0 + threadIdx.x], v0 + threadIdx.x);
+  for (int v = vtail + threadIdx.x; v < v1; v += kVerifyThreads) best = max_key<L>(best, src[v], v);
   best = warp_max_u64(best);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
   __syncthreads();

@@ -133,6 +133,7 @@ struct GemvParams {
   const void* z_src;
   int z_rows_per_b, z_pos_off;
   void* mid_out;
+  void* s_out;  // optional trace: s[b * E + e] (rounded), as the epilogue uses it
   // EPI_GH
   void* gh_out;
   const void* b_hh;
@@ -307,7 +308,7 @@ __device__ __noinline__ void prefix_argmax_chunk(unsigned long long* slots, int 
     const int pos = (int)(gn % kpos);
     if (pos < npre) {  // uniform across the warp
       const float fv = IO::to_f(vals[j]);
-      unsigned long long key = (valid && !isnan(fv)) ? argmax_key(fv, vocab_row) : 0ull;
+      unsigned long long key = valid ? argmax_key(fv, vocab_row) : 0ull;
       key = warp_max_u64(key);
       if (lane == 0 && key) atomicMax(slots + (gn / kpos) * nslots + pos, key);
     }
@@ -449,7 +450,9 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
       for (int j = 0; j < 16; ++j) {
         const int b = ch * 16 + j;
         if (b < p.B && valid) {
-          const float s = IO::to_f(IO::from_f(v[j]));
+          const T s_rounded = IO::from_f(v[j]);
+          if (p.s_out) ((T*)p.s_out)[(size_t)b * p.E + row] = s_rounded;
+          const float s = IO::to_f(s_rounded);
           const float z = zv[j];
           const float pre = z + s;
           const float mid = pre * sigmoidf_(pre);
@@ -489,7 +492,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           unsigned long long key = 0ull;
           if (b < p.B && valid && ch < nchunks) {
             const float logit = v[2 * i] + v[2 * i + 1] + bias + basev[i];
-            if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
+            key = argmax_key(logit, (uint32_t)(p.v_off + row));
           }
           k[b] = key;
         }
@@ -518,7 +521,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
             float logit = v[2 * b] + v[2 * b + 1];
             logit += bias;
             logit += IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
-            if (!isnan(logit)) key = argmax_key(logit, (uint32_t)(p.v_off + row));
+            key = argmax_key(logit, (uint32_t)(p.v_off + row));
           }
           key = warp_max_u64(key);
           if (lane == 0) red[q * kMaxBatch + b] = key;

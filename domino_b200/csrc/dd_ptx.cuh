@@ -204,9 +204,12 @@ __device__ __forceinline__ uint32_t float_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 // (value, index) -> 64-bit word whose unsigned max is the argmax with the
-// lowest index winning ties.  0 is below every real key.
+// lowest index winning ties.  0 is below every real key.  A NaN of either sign
+// gets the top value key, above +inf, so that the first NaN wins the way
+// torch.argmax treats NaN (greater than every number, lowest index on ties).
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
-  return (static_cast<unsigned long long>(float_key(v)) << 32) | static_cast<unsigned long long>(0xFFFFFFFFu - idx);
+  const uint32_t hi = (v != v) ? 0xFFFFFFFFu : float_key(v);
+  return (static_cast<unsigned long long>(hi) << 32) | static_cast<unsigned long long>(0xFFFFFFFFu - idx);
 }
 __device__ __forceinline__ uint32_t argmax_key_index(unsigned long long k) {
   return 0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull);

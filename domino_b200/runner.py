@@ -347,6 +347,42 @@ class DraftCorrectionGraphRunner:
         )
         return verify, base_logits_out
 
+    @torch.inference_mode()
+    def rollout_trace(self, prefix_ids: torch.Tensor, parallel_hiddens: torch.Tensor, base_logits: torch.Tensor):
+        """One eager rollout (like ``__call__``) that also returns its per-step states.
+
+        Returns ``(tokens [B, S], states)`` with ``states`` holding, in the
+        weight dtype (code/kernel/domino.py:381-431):
+          ``z``  [B, S, E]        z projection (+ fc1 bias);
+          ``h``  [P + S - 1, B, G] GRU state after each prefix token, then
+                                   after the GRU step of each draft step;
+          ``gh`` [P + S - 2, B, 3G] ``h W_hh^T + b_hh`` fed to those GRU steps
+                                   (prefix tokens after the first, then draft steps);
+          ``s``  [S, B, E]        s projections.
+        P = ``prefix_token_count``.  Unsharded runners only.
+        """
+        if self.world > 1:
+            raise ValueError("rollout_trace needs an unsharded runner")
+        B, S, P, E = self.batch_size, self.steps, self.prefix_token_count, self._fc1.shape[0]
+        G, dev, dt = self.gru_hidden_dim, self.device, self.dtype
+        st = {
+            "z": torch.zeros(B, S, E, dtype=dt, device=dev),
+            "h": torch.zeros(P + S - 1, B, G, dtype=dt, device=dev),
+            "gh": torch.zeros(max(P + S - 2, 1), B, 3 * G, dtype=dt, device=dev),
+            "s": torch.zeros(S, B, E, dtype=dt, device=dev),
+        }
+        tr = _lib.DDTrace(z=st["z"].data_ptr(), h=st["h"].data_ptr(), gh=st["gh"].data_ptr(), s=st["s"].data_ptr())
+        self.static_prefix_ids.copy_(prefix_ids)
+        self.static_parallel_hiddens.copy_(parallel_hiddens)
+        self.static_base_logits.copy_(base_logits)
+        _lib.check(self._lib.dd_set_trace(self._h, ctypes.byref(tr)), self._h, "dd_set_trace")
+        try:
+            self._forward_impl()
+        finally:
+            self._lib.dd_set_trace(self._h, None)
+        st["gh"] = st["gh"][: P + S - 2]
+        return self.static_out.clone(), st
+
     def status(self) -> int:
         """Synchronise and return (and clear) the device status bits (DD_STATUS_*)."""
         return _lib.check(self._lib.dd_get_status(self._h), self._h, "dd_get_status")
@@ -357,8 +393,20 @@ class DraftCorrectionGraphRunner:
         return self._table
 
     def close(self):
+        """Free the handle.  A vocab-sharded runner must be closed by every rank
+        (the call contains a barrier over the default process group)."""
         if getattr(self, "_h", None):
             self.graph = None
+            if self.world > 1:
+                # Peers publish argmax words and s / gh flags into this rank's
+                # exchange buffer with system-scope stores: every rank drains
+                # its own work and waits for all the others before any buffer
+                # is unmapped or freed (the mirror of the setup barrier).
+                import torch.distributed as dist
+
+                torch.cuda.synchronize(self.device)
+                if dist.is_available() and dist.is_initialized():
+                    dist.barrier()
             for p in getattr(self, "_peer_ptrs", []):
                 self._lib.dd_ipc_close(self.device.index, p)
             self._peer_ptrs = []
@@ -366,7 +414,12 @@ class DraftCorrectionGraphRunner:
             self._h = None
 
     def __del__(self):
+        # A finaliser cannot join a barrier (ranks collect garbage at different
+        # times), so a vocab-sharded runner that was never closed keeps its
+        # exchange buffer until the process exits rather than freeing memory
+        # that a peer may still write into.
         try:
-            self.close()
+            if getattr(self, "world", 1) == 1:
+                self.close()
         except Exception:
             pass

@@ -50,7 +50,11 @@ extern "C" {
 /* Device status bits (dd_get_status). */
 #define DD_STATUS_TIMEOUT 1u       /* a bounded wait inside a kernel gave up */
 #define DD_STATUS_BAD_TOKEN 2u     /* a token id was outside [0, vocab) and was clamped */
-#define DD_STATUS_NO_ARGMAX 4u     /* an argmax saw no finite candidate (all NaN) */
+#define DD_STATUS_NO_ARGMAX 4u     /* an argmax saw no candidate at all */
+
+/* Argmax semantics, in every kernel here: the lowest index wins a tie, and a
+ * NaN of either sign ranks above every number (the first NaN wins), as
+ * torch.argmax does. */
 
 typedef struct dd_handle dd_handle;
 
@@ -148,10 +152,22 @@ int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel
  *     the call clears what must start at zero.  Calls whose work overlaps on
  *     the GPU (two streams, or two host threads on one device) race on it:
  *     order them on one stream.
- *   - Errors are reported through dd_last_error(NULL). */
+ *   - Host-side errors are returned at once, with a reason in
+ *     dd_last_error(NULL).  What the kernels find while running (a bounded
+ *     wait that gave up, a clamped token id) collects in a status word of
+ *     the same static array: read it with dd_noalloc_status. */
 int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int device, const int64_t* prefix_ids,
                        const void* parallel_hiddens, const void* base_logits, int64_t* out_tokens,
                        void* stream);
+
+/* Status of the allocation-free calls on `device` (no counterpart in the
+ * reference): waits for the device, then returns and clears the DD_STATUS_*
+ * bits that dd_rollout_noalloc's kernels have set since the last read (0 =
+ * every call ran clean; 0 as well when no such call has run).  Negative on a
+ * CUDA error.  A caller without a handle has no dd_get_status; this is the
+ * one way it learns that a rollout timed out (DD_STATUS_TIMEOUT: discard its
+ * tokens) or that a prefix id was out of range.  It allocates nothing. */
+int dd_noalloc_status(int device);
 
 /* Greedy acceptance (code/dflash.py:472-485) for every row:
  *   verify_ids [B, K1] int64, posterior [B, K1] int64 (K1 = draft tokens + 1)
@@ -203,8 +219,9 @@ int dd_set_vocab_shard(dd_handle* h, int32_t rank, int32_t world, int64_t vocab_
 int dd_set_exchange_timeout(dd_handle* h, uint64_t timeout_ns);
 
 /* The target-side half of code/dflash.py:472-485 fused into one pass:
- * posterior[b, j] = argmax_v target_logits[b, j, v] (lowest index on ties, as
- * torch.argmax) and the greedy acceptance of verify_ids against it; the
+ * posterior[b, j] = argmax_v target_logits[b, j, v] (lowest index on ties and
+ * NaN above every number, as torch.argmax) and the greedy acceptance of
+ * verify_ids against it; the
  * [B, k1, V] logits are read once and no intermediate is written.
  *   target_logits [B, k1, V] (DD_BF16, DD_FP16 or DD_F32), V = cfg.vocab
  *   verify_ids [B, k1] int64; posterior_out [B, k1] int64;
@@ -213,6 +230,34 @@ int dd_set_exchange_timeout(dd_handle* h, uint64_t timeout_ns);
 int dd_verify_accept(dd_handle* h, const void* target_logits, int32_t logits_dtype, int32_t k1,
                      const int64_t* verify_ids, int64_t* posterior_out, int32_t* accept_out,
                      int64_t* bonus_out, void* stream);
+
+/* Debugging and parity aid (no counterpart in the reference): the per-step
+ * states of the rollout, in the weight dtype, as the kernels compute and use
+ * them.  Device buffers; any of them may be NULL.  With P = prefix_tokens
+ * (plus the pure-draft prefix positions for dd_draft_block) and S = steps:
+ *   z  [B, K, E]          z projection (+ fc1 bias); K = S for dd_rollout,
+ *                         p + S for dd_draft_block
+ *   h  [P + S - 1, B, G]  GRU state after prefix token j (entries 0..P-1,
+ *                         entry P-1 = the state entering draft step 0), then
+ *                         after the GRU step of draft step t (entry P + t)
+ *   gh [P - 1 + S - 1, B, 3G]  h W_hh^T + b_hh of prefix token j >= 1 (entry
+ *                         j - 1), then of draft step t (entry P - 1 + t)
+ *   s  [S, B, E]          s projection h W_s^T of draft step t (entry t)
+ * The mapping of code/kernel/domino.py:381-431: z = z_part_all, the h entry
+ * P - 1 = gru_hidden after the prefix GRU, s = s_proj, gh = the F.linear of
+ * line 420 and the h entries >= P = the _fused_gru_cell outputs. */
+typedef struct dd_trace {
+  void* z;
+  void* h;
+  void* gh;
+  void* s;
+} dd_trace;
+
+/* While a trace is set (t != NULL), dd_rollout and dd_draft_block also copy
+ * every state above into it, on the call's stream, between their launches
+ * (one kernel per phase; the persistent rollout is not used).  NULL stops
+ * tracing.  Unsharded handles only.  Slower: for tests and debugging. */
+int dd_set_trace(dd_handle* h, const dd_trace* t);
 
 /* Launch kinds reported by dd_read_timing. */
 #define DD_PHASE_Z 1      /* z = parallel_hiddens @ W_z^T */

@@ -178,11 +178,15 @@ def orderable_key(v: np.ndarray) -> np.ndarray:
 def packed_argmax_key(v: np.ndarray, idx: np.ndarray) -> np.ndarray:
     """64-bit key whose unsigned max is the (value, lowest index) argmax.
 
-    High word: order-preserving image of the fp32 logit; low word:
-    ``0xFFFFFFFF - idx`` so that, among equal values, the lowest index wins.
-    This is the word the GPU kernels combine with ``atomicMax``.
+    High word: order-preserving image of the fp32 logit, and the top value
+    for a NaN of either sign (``torch.argmax`` and ``np.argmax`` rank NaN
+    above every number and return the first one, code/dflash.py:472); low
+    word: ``0xFFFFFFFF - idx`` so that, among equal values, the lowest index
+    wins.  This is the word the GPU kernels combine with ``atomicMax``.
     """
-    hi = orderable_key(v).astype(np.uint64) << np.uint64(32)
+    v = np.asarray(v, dtype=np.float32)
+    hi32 = np.where(np.isnan(v), np.uint32(0xFFFFFFFF), orderable_key(v)).astype(np.uint32)
+    hi = hi32.astype(np.uint64) << np.uint64(32)
     lo = (np.uint64(0xFFFFFFFF) - np.asarray(idx, dtype=np.uint64)) & np.uint64(0xFFFFFFFF)
     return hi | lo
 
@@ -250,11 +254,14 @@ def build_table(embed: np.ndarray, w_ih: np.ndarray, b_ih: Optional[np.ndarray],
     return linear(embed, w_ih, b_ih, dtype)
 
 
-def prefix_gru(w: DraftWeights, prefix_ids: np.ndarray) -> np.ndarray:
+def prefix_gru(w: DraftWeights, prefix_ids: np.ndarray, states: Optional[dict] = None) -> np.ndarray:
     """h0 = GRU over ``embed(prefix_ids)`` from a zero state, domino.py:387-391.
 
     Restated as ``gi = table[token]``, ``gh = W_hh h + b_hh``, fused cell, one
-    prefix token at a time.  Returns ``[B, G]`` in the state dtype.
+    prefix token at a time.  Returns ``[B, G]`` in the state dtype.  With
+    ``states`` (a dict) it also records ``states["h"]``, the state after each
+    prefix token, and ``states["gh"]``, the ``gh`` of every token after the
+    first (the first token's is ``b_hh``, from the zero state).
     """
     prefix_ids = np.asarray(prefix_ids, dtype=np.int64)
     B, P = prefix_ids.shape
@@ -264,6 +271,10 @@ def prefix_gru(w: DraftWeights, prefix_ids: np.ndarray) -> np.ndarray:
         gi = table[prefix_ids[:, j]]
         gh = linear(h, w.w_hh, w.b_hh, w.dtype)
         h = gru_cell(gi, gh, h, w.dtype)
+        if states is not None:
+            states.setdefault("h", []).append(h.copy())
+            if j > 0:
+                states.setdefault("gh", []).append(gh)
     return h
 
 
@@ -292,6 +303,9 @@ class RolloutTrace:
     s_proj: list = field(default_factory=list)
     z_part: Optional[np.ndarray] = None   # [B, S, E]
     logits: list = field(default_factory=list)
+    gh: list = field(default_factory=list)        # per step t < S-1, h_t W_hh^T + b_hh (domino.py:420)
+    prefix_h: list = field(default_factory=list)  # state after each prefix token
+    prefix_gh: list = field(default_factory=list)  # gh of each prefix token after the first
 
 
 def rollout(
@@ -316,14 +330,16 @@ def rollout(
     base = np.asarray(base_logits, dtype=np.float32)
     B, S, _ = ph.shape
     z_part = linear(ph, w.w_z, w.fc1_bias, dtype)               # domino.py:381-385
-    h = prefix_gru(w, prefix_ids)                               # domino.py:387-391
+    pre: dict = {}
+    h = prefix_gru(w, prefix_ids, pre)                          # domino.py:387-391
     table = w.get_table()
     tokens = np.zeros((B, S), np.int64)
     fed = np.zeros((B, S), np.int64)
     gaps = np.zeros((B, S), np.float32)
     chosen = np.zeros((B, S), np.float32)
     top = np.zeros((B, S), np.float32)
-    trace = RolloutTrace(tokens, gaps, chosen, top, fed, h0=h.copy(), z_part=z_part)
+    trace = RolloutTrace(tokens, gaps, chosen, top, fed, h0=h.copy(), z_part=z_part,
+                         prefix_h=pre.get("h", []), prefix_gh=pre.get("gh", []))
     for t in range(S):
         trace.h.append(h.copy())
         s_proj = linear(h, w.w_s, None, dtype)                  # domino.py:397
@@ -340,7 +356,8 @@ def rollout(
         chosen[:, t] = logits[np.arange(B), cur]
         if t + 1 < S:                                           # domino.py:416-431
             gi = table[cur]
-            gh = linear(h, w.w_hh, w.b_hh, dtype)
+            gh = linear(h, w.w_hh, w.b_hh, dtype)                # domino.py:420
+            trace.gh.append(gh)
             h = gru_cell(gi, gh, h, dtype)
     return trace
 

@@ -1,10 +1,10 @@
 """Generate the golden fixtures under tests/golden/ by running the reference.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference`` (override with ``DOMINO_REFERENCE``); the fixtures it
-writes are committed, so nothing else needs the reference at run time.
+Run where a checkout of the reference (jianuo-huang/Domino) is available,
+naming its root in ``DOMINO_REFERENCE`` (required); the fixtures it writes are
+committed, so nothing else needs the reference at run time.
 
-    python tests/golden/make_golden.py
+    DOMINO_REFERENCE=/path/to/Domino python tests/golden/make_golden.py
 
 What it runs, all on CPU:
 
@@ -31,7 +31,9 @@ import sys
 from pathlib import Path
 
 os.environ.setdefault("TRITON_INTERPRET", "1")
-REF = Path(os.environ.get("DOMINO_REFERENCE", "/root/reference")) / "code"
+if not os.environ.get("DOMINO_REFERENCE"):
+    sys.exit("set DOMINO_REFERENCE to the root of a Domino checkout (the directory holding code/)")
+REF = Path(os.environ["DOMINO_REFERENCE"]) / "code"
 OUT = Path(__file__).resolve().parent
 
 import numpy as np  # noqa: E402

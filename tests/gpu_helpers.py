@@ -2,6 +2,8 @@
 reference's layout, oracle weights, and the teacher-forced token check."""
 from __future__ import annotations
 
+import os
+
 import numpy as np
 import torch
 import torch.nn as nn
@@ -10,6 +12,35 @@ from oracle import draft_oracle as O
 from tests.fixtures import as_f32
 
 TOL = 2e-2  # atol = rtol: bf16 logits/states, and the top-2 gap below which an argmax may differ
+
+# One line per parity check, printed at the end of the run (tests/conftest.py).
+PARITY_LOG: list = []
+
+
+def _test_name() -> str:
+    name = os.environ.get("PYTEST_CURRENT_TEST", "?").split(" ")[0]
+    return name.split("::", 1)[-1]
+
+
+def log_parity(text: str) -> None:
+    PARITY_LOG.append(f"{_test_name()}: {text}")
+
+
+def compare_states(label, got, ref, tol=TOL):
+    """Assert ``|got - ref| <= tol + tol * |ref|`` elementwise (bf16 states and
+    logits) and return (max abs difference, fraction of bit-identical values)."""
+    g = got.float() if torch.is_tensor(got) else torch.from_numpy(np.asarray(got, np.float32))
+    r = ref.float() if torch.is_tensor(ref) else torch.from_numpy(np.asarray(ref, np.float32))
+    g = g.to(r.device)
+    assert g.shape == r.shape, (label, tuple(g.shape), tuple(r.shape))
+    if g.numel() == 0:
+        return 0.0, 1.0
+    diff = (g - r).abs()
+    bad = diff > tol + tol * r.abs()
+    assert not bool(bad.any()), (
+        f"{label}: {int(bad.sum())} of {bad.numel()} values beyond atol=rtol={tol}; "
+        f"max |diff| {float(diff.max()):.4g} at {np.unravel_index(int(diff.argmax()), tuple(diff.shape))}")
+    return float(diff.max()), float((g == r).float().mean())
 
 
 class DraftHead(nn.Module):
@@ -106,6 +137,8 @@ def teacher_forced_check(w: O.DraftWeights, prefix, ph, base, gpu_tokens, min_ex
         f"gpu {tok[bad]}, oracle {tr.tokens[bad]}, slack {slack[bad]}"
     )
     frac = float(exact.mean())
+    worst = float(slack[~exact].max()) if (~exact).any() else 0.0
+    log_parity(f"tokens {int(exact.sum())}/{exact.size} exact ({frac:.3f}), worst near-tie slack {worst:.3g}")
     assert frac >= min_exact, f"only {frac:.3f} of the tokens are exact"
     return frac, tr
 

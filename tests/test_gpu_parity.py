@@ -273,3 +273,30 @@ def test_spec_generate_trace_replay():
         teacher_forced_check(w, prefix, ph, base, out, min_exact=0.8)
         acc, bonus = r.accept(torch.from_numpy(fx["verify_ids"][i]).cuda(), torch.from_numpy(fx["posterior"][i]).cuda())
         assert int(acc[0]) + 1 == int(fx["acceptance_lengths"][i])
+
+
+@pytest.mark.parametrize("B", [2, 6])  # the per-row (B <= 4) and the butterfly (B > 4) fc2 argmax
+def test_nan_logits_win_like_torch_argmax(B):
+    """NaN base logits: the draft token is the first NaN's index, as
+    torch.argmax returns it (the reference's PyTorch branch, domino.py:409);
+    an all-NaN hidden state makes an all-NaN base row, so the pure-draft
+    prefix token is 0."""
+    H, G, E, V, S, P = 128, 128, 192, 1500, 13, 2
+    draft, target = random_modules(H, G, E, V, seed=71 + B, fc2_std=0.08)
+    r = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=B)
+    b = B - 1
+    base[b, 4, 900] = float("nan")
+    base[b, 4, 333] = float("nan")
+    base[0, 6, V - 1] = float("nan")
+    out = r(prefix, ph, base)
+    assert r.status() == 0
+    assert int(out[b, 4]) == 333 and int(out[0, 6]) == V - 1
+    K = P - 1 + S
+    g = torch.Generator().manual_seed(3)
+    ph2 = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    ph2[b, 0, :] = float("nan")
+    last = torch.randint(0, V, (B,), generator=g).cuda()
+    verify, base_out = r.draft_block(last, ph2)
+    assert r.status() == 0
+    assert bool(torch.isnan(base_out[b, 0]).all()) and int(verify[b, 1]) == 0

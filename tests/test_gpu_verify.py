@@ -63,3 +63,26 @@ def test_verify_accept_full_vocab_and_full_acceptance():
     assert acc.tolist() == [K1 - 1] * B
     assert torch.equal(bonus, post_ref[:, -1])
     r.close()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_verify_accept_nan_ranks_first_like_torch_argmax(dtype):
+    """A NaN logit wins over every number and the first NaN wins, as in
+    torch.argmax (code/dflash.py:472); the odd V leaves rows unaligned, so the
+    scalar head and tail of the vector loop see NaNs too."""
+    B, K1, V = 3, 16, 20011
+    r = _runner(B, V)
+    logits, verify, _ = _case(B, K1, V, dtype, 7)
+    logits[0, 2, 9000] = float("nan")
+    logits[0, 2, 7] = float("nan")          # the first NaN of the row
+    logits[1, 5, V - 1] = float("nan")      # last element
+    logits[2, 0, 0] = float("inf")
+    logits[2, 0, 3] = float("nan")          # NaN above +inf
+    logits[2, 7, :] = float("nan")          # all NaN: index 0
+    post_ref = torch.argmax(logits.float(), dim=-1)
+    post, acc, bonus = r.verify_accept(logits, verify)
+    assert r.status() == 0
+    assert torch.equal(post, post_ref)
+    assert post[0, 2] == 7 and post[1, 5] == V - 1 and post[2, 0] == 3 and post[2, 7] == 0
+    assert np.array_equal(post.cpu().numpy(), np.argmax(logits.float().cpu().numpy(), axis=-1))
+    r.close()

@@ -39,6 +39,17 @@ def test_packed_key_order():
     assert int(np.argmax(O.packed_argmax_key(w, np.arange(8)))) == 0
 
 
+def test_packed_key_nan_is_the_maximum_like_torch_argmax():
+    """NaN ranks above +inf and the first NaN wins, as in torch.argmax."""
+    import torch
+
+    for v in ([1.0, np.nan, np.inf, -np.nan, 5.0], [-np.nan, 2.0, np.nan], [np.inf, 3.0, -np.nan]):
+        v = np.asarray(v, np.float32)
+        keys = O.packed_argmax_key(v, np.arange(v.size))
+        expect = int(torch.argmax(torch.from_numpy(v)))
+        assert int(np.argmax(keys)) == expect == int(O.argmax_lowest(v))
+
+
 @pytest.mark.parametrize("case", ROLLOUT_CASES)
 def test_table_and_z_part(case):
     fx = load(case)
@@ -73,9 +84,14 @@ def test_rollout_teacher_forced_states(case):
         ok, err = close(tr.s_proj[t], s_ref[:, t])
         assert ok, (t, err)
     h_ref = as_f32(fx["h_out"])
+    gh_ref = as_f32(fx["gh"])
     for t in range(S - 1):
         ok, err = close(tr.h[t + 1], h_ref[:, t])
         assert ok, (t, err)
+        ok, err = close(tr.gh[t], gh_ref[:, t])
+        assert ok, (t, err)
+    ok, err = close(tr.prefix_h[-1], as_f32(fx["h0"]))
+    assert ok, err
     # Own argmax vs the reference's token at every step: equal, or a near-tie.
     diff = tr.tokens != ref_tok
     assert np.all(tr.gaps[diff] < TOL), (np.argwhere(diff), tr.gaps[diff])
@@ -122,3 +138,29 @@ def test_spec_generate_trace(case):
         a, bonus = O.accept(verify, fx["posterior"][i])
         assert int(a[0]) + 1 == int(fx["acceptance_lengths"][i])
         assert int(bonus[0]) == int(fx["posterior"][i][0, a[0]])
+
+
+@pytest.mark.parametrize("case", ROLLOUT_CASES)
+def test_torch_branch_matches_reference_pytorch_branch(case):
+    """The CPU benchmark leg (oracle/torch_branch.py) reproduces the tokens of
+    the reference's PyTorch branch, recorded by running it (tokens_torch)."""
+    import torch
+
+    from oracle import torch_branch as TB
+    from tests.gpu_helpers import modules_from_fixture
+
+    fx = load(case)
+    draft, target = modules_from_fixture(fx, device="cpu")
+    if str(fx["dtype"]) == "fp32":
+        draft, target = draft.float(), target.float()
+        for mod, key in ((draft.embed_proj[0], "fc1"), (draft.embed_proj[2], "fc2")):
+            mod.weight.data.copy_(torch.from_numpy(as_f32(fx[key])))
+        draft.prefix_gru.weight_ih_l0.data.copy_(torch.from_numpy(as_f32(fx["w_ih"])))
+        draft.prefix_gru.weight_hh_l0.data.copy_(torch.from_numpy(as_f32(fx["w_hh"])))
+        target.model.embed_tokens.weight.data.copy_(torch.from_numpy(as_f32(fx["embed"])))
+    dt = draft.embed_proj[0].weight.dtype
+    w = TB.head_from_modules(draft, target)
+    assert torch.equal(w.table.float(), torch.from_numpy(as_f32(fx["table"])))
+    out = TB.rollout(w, torch.from_numpy(fx["prefix_ids"]), torch.from_numpy(as_f32(fx["parallel_hiddens"])).to(dt),
+                     torch.from_numpy(as_f32(fx["base_logits"])).to(dt))
+    assert np.array_equal(out.numpy(), fx["tokens_torch"])

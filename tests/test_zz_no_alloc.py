@@ -45,8 +45,32 @@ def test_noalloc_rollout_matches_handle_rollout_twice():
         rc = lib.dd_rollout_noalloc(ctypes.byref(cfg), ctypes.byref(runner._weights), 0, prefix.data_ptr(),
                                     ph.data_ptr(), base.data_ptr(), out.data_ptr(), stream)
         assert rc == _lib.DD_OK, lib.dd_last_error(None)
-        torch.cuda.synchronize()
+        # the kernels' own status (bounded waits, token ids): clean
+        assert lib.dd_noalloc_status(0) == 0
         assert torch.equal(out, expected), (call, out, expected)
+
+
+def test_noalloc_status_reports_a_clamped_prefix_id_once():
+    """A caller without a handle still learns what the kernels found: an
+    out-of-range prefix id is clamped and flagged in the static status word,
+    which dd_noalloc_status returns and clears."""
+    from domino_b200 import DraftCorrectionGraphRunner, _lib
+
+    lib = _lib.load()
+    B, H, G, E, V, S, P = 2, 64, 64, 96, 700, 15, 1
+    draft, target = random_modules(H, G, E, V, seed=41)
+    runner = DraftCorrectionGraphRunner(draft, target, B, S, H, G, V, P, torch.device("cuda", 0), use_graph=False)
+    cfg = _lib.DDConfig(batch=B, steps=S, hidden=H, gru_hidden=G, emb_dim=E, vocab=V, prefix_tokens=P,
+                        dtype=_lib.DD_BF16)
+    prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=1)
+    prefix[0, 0] = V + 5
+    out = torch.empty(B, S, dtype=torch.long, device="cuda")
+    rc = lib.dd_rollout_noalloc(ctypes.byref(cfg), ctypes.byref(runner._weights), 0, prefix.data_ptr(),
+                                ph.data_ptr(), base.data_ptr(), out.data_ptr(),
+                                torch.cuda.current_stream().cuda_stream)
+    assert rc == _lib.DD_OK, lib.dd_last_error(None)
+    assert lib.dd_noalloc_status(0) == _lib.DD_STATUS_BAD_TOKEN
+    assert lib.dd_noalloc_status(0) == 0  # reading cleared it
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
