@@ -31,6 +31,7 @@
 #include "../../include/domino_draft.h"
 #include "dd_cell.cuh"
 #include "dd_gemv.cuh"
+#include "dd_gemv_f32.cuh"
 #include "dd_rollout.cuh"
 
 using namespace dd;
@@ -56,6 +57,7 @@ struct dd_handle {
   dd_config cfg{};
   dd_weights w{};
   bool have_weights = false;
+  int es = 2;   // bytes per activation / weight element: 2 (bf16, fp16) or 4 (fp32)
   int N1 = 16;  // MMA N of the h operand: batch rows padded to 16
   int N2 = 16;  // MMA N of the mid operand: 2 * batch (hi, lo) padded to 16
   int nslots = 0;
@@ -243,8 +245,8 @@ struct Launch {
 
 // Fill the pass-independent launch fields of a gemv phase and launch it.
 template <typename T, int kPhase>
-int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, const CUtensorMap& b, GemvParams p,
-                PhaseClass cls, bool allow_split, cudaStream_t st) {
+int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, const CUtensorMap& b, GemvParams p,
+                   PhaseClass cls, bool allow_split, cudaStream_t st) {
   p.KC = ceil_div(p.K, kChunkK);
   int tiles = 0;
   for (int s = 0; s < p.nseg; ++s) {
@@ -306,6 +308,40 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
   Launch L(dim3(grid), dim3(kThreads), smem, st);
   DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, gemv_stream_kernel<T, kPhase>, a0, a1 ? *a1 : a0, b, p));
   return timing_end(h, st);
+}
+
+// fp32 heads: the phase's rows through gemv_f32_kernel, in launches of at
+// most kF32MaxN X rows (the weights are read once per launch).
+template <int kPhase>
+int launch_gemv_f32(dd_handle* h, GemvParams p, cudaStream_t st) {
+  int rows = 0;
+  for (int s = 0; s < p.nseg; ++s) rows += p.seg[s].rows;
+  p.status = h->status;
+  const int n_begin = p.n_off;
+  const int n_total = kPhase == PH_FC2 ? p.B : p.n_valid;
+  const int grid = std::max(1, ceil_div(rows, kF32RowsPerCta));
+  for (int n0 = 0; n0 < n_total; n0 += kF32MaxN) {
+    p.n_off = n_begin + n0;
+    p.n_valid = std::min(kF32MaxN, n_total - n0);
+    int rc = timing_begin(h, kPhase, st);
+    if (rc) return rc;
+    Launch L(dim3(grid), dim3(kF32Threads), 0, st);
+    DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, gemv_f32_kernel<kPhase>, p));
+    rc = timing_end(h, st);
+    if (rc) return rc;
+  }
+  return DD_OK;
+}
+
+// One contraction phase: tcgen05 weight streaming for bf16 / fp16 heads,
+// CUDA-core fp32 FMA for fp32 heads.
+template <typename T, int kPhase>
+int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, const CUtensorMap& b, GemvParams p,
+                PhaseClass cls, bool allow_split, cudaStream_t st) {
+  if constexpr (std::is_same<T, float>::value)
+    return launch_gemv_f32<kPhase>(h, p, st);
+  else
+    return launch_gemv_tc<T, kPhase>(h, a0, a1, b, p, cls, allow_split, st);
 }
 
 Exchange make_exchange(const dd_handle* h);
@@ -417,7 +453,7 @@ int launch_gather(dd_handle* h, int slot, bool with_gh, cudaStream_t st) {
 // from a scratch buffer into entry `idx` of a caller trace array.
 int trace_copy(dd_handle* h, void* dst, int idx, const void* src, long long rows, long long cols, cudaStream_t st) {
   if (!h->tracing || !dst) return DD_OK;
-  const size_t bytes = (size_t)rows * cols * 2;
+  const size_t bytes = (size_t)rows * cols * h->es;
   DD_CUDA(h, cudaMemcpyAsync(static_cast<uint8_t*>(dst) + (size_t)idx * bytes, src, bytes, cudaMemcpyDeviceToDevice, st));
   return DD_OK;
 }
@@ -429,10 +465,19 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
   const int rows = c.batch * positions;
   CUtensorMap tm_x;
   const int n_pass = std::min(256, round_up(rows, 16));
-  int rc = encode_kmajor(h, &tm_x, ph, c.dtype, c.hidden, rows, c.hidden, n_pass);
-  if (rc) return rc;
+  int rc = DD_OK;
+  if constexpr (!std::is_same<T, float>::value) {
+    rc = encode_kmajor(h, &tm_x, ph, c.dtype, c.hidden, rows, c.hidden, n_pass);
+    if (rc) return rc;
+  }
   for (int n_off = 0; n_off < rows; n_off += 256) {
     GemvParams p = base_params(h);
+    p.x32 = static_cast<const float*>(ph);
+    p.x32_ld = c.hidden;
+    p.w32[0] = static_cast<const float*>(base_out ? h->w.lm_head : h->w.fc1);
+    p.w32_ld[0] = base_out ? h->w.lm_head_ld : h->w.fc1_ld;
+    p.w32[1] = static_cast<const float*>(h->w.fc1);
+    p.w32_ld[1] = h->w.fc1_ld;
     const int n_valid = std::min(256, rows - n_off);
     p.N = n_pass;  // == the TMA box height, so expect_tx matches the bytes every load delivers
     p.n_off = n_off;
@@ -503,6 +548,10 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
     p.gh_out = h->ghbuf;
     p.b_hh = h->w.b_hh;
     p.packed[0] = static_cast<const uint8_t*>(h->pk_whh);
+    p.w32[0] = static_cast<const float*>(h->w.w_hh);
+    p.w32_ld[0] = h->w.w_hh_ld;
+    p.x32 = static_cast<const float*>(h->hbuf[cur]);
+    p.x32_ld = c.gru_hidden;
     rc = launch_gemv<T, PH_GH>(h, h->tm_whh, nullptr, h->tm_h[cur], p, PhaseClass::Small, true, st);
     if (!rc) rc = trace_copy(h, h->trace.gh, j - 1, h->ghbuf, c.batch, 3LL * c.gru_hidden, st);
     if (rc) return rc;
@@ -554,9 +603,16 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.mid_out = h->midbuf;
       p.gh_out = h->ghbuf;
       p.b_hh = h->w.b_hh;
-      if (h->tracing && h->trace.s) p.s_out = static_cast<uint8_t*>(h->trace.s) + (size_t)t * c.batch * c.emb_dim * 2;
+      if (h->tracing && h->trace.s)
+        p.s_out = static_cast<uint8_t*>(h->trace.s) + (size_t)t * c.batch * c.emb_dim * h->es;
       p.packed[0] = static_cast<const uint8_t*>(h->pk_ws);
       p.packed[1] = static_cast<const uint8_t*>(h->pk_whh);
+      p.w32[0] = static_cast<const float*>(h->w.fc1) + c.hidden;  // W_s = fc1[:, H:]
+      p.w32_ld[0] = h->w.fc1_ld;
+      p.w32[1] = static_cast<const float*>(h->w.w_hh);
+      p.w32_ld[1] = h->w.w_hh_ld;
+      p.x32 = static_cast<const float*>(h->hbuf[cur]);
+      p.x32_ld = c.gru_hidden;
       rc = launch_gemv<T, PH_SGH>(h, h->tm_ws, last ? nullptr : &h->tm_whh, h->tm_h[cur], p, PhaseClass::Small, true, st);
       if (!rc && !last)
         rc = trace_copy(h, h->trace.gh, n_prefix_total - 1 + t, h->ghbuf, c.batch, 3LL * c.gru_hidden, st);
@@ -584,6 +640,10 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.base_rows_per_b = positions;
       p.base_pos_off = npre;
       p.fc2_bias = h->w.fc2_bias;
+      p.w32[0] = static_cast<const float*>(h->w.fc2);
+      p.w32_ld[0] = h->w.fc2_ld;
+      p.x32 = static_cast<const float*>(h->midbuf);  // fp32 heads: mid is [B, E] fp32
+      p.x32_ld = c.emb_dim;
       rc = launch_gemv<T, PH_FC2>(h, h->tm_fc2, nullptr, h->tm_mid, p, PhaseClass::Big, true, st);
       if (rc) return rc;
     }
@@ -864,7 +924,8 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
     return fail(nullptr, DD_EINVAL, "bad shape");
   if (c.hidden % 8 || c.gru_hidden % 8 || c.emb_dim % 8)
     return fail(nullptr, DD_EINVAL, "hidden, gru_hidden and emb_dim must be multiples of 8");
-  if (c.dtype != DD_BF16 && c.dtype != DD_FP16) return fail(nullptr, DD_EINVAL, "dtype must be DD_BF16 or DD_FP16");
+  if (c.dtype != DD_BF16 && c.dtype != DD_FP16 && c.dtype != DD_F32)
+    return fail(nullptr, DD_EINVAL, "dtype must be DD_BF16, DD_FP16 or DD_F32");
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, device) != cudaSuccess)
     return fail(nullptr, DD_ECUDA, "cannot query device %d", device);
@@ -874,6 +935,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   dd_handle* h = new dd_handle();
   h->device = device;
   h->cfg = c;
+  h->es = c.dtype == DD_F32 ? 4 : 2;
   h->num_sms = prop.multiProcessorCount;
   h->N1 = round_up(c.batch, 16);
   h->N2 = round_up(2 * c.batch, 16);
@@ -889,8 +951,8 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
     bytes = (bytes + 255) & ~size_t(255);
     h->xmid_off = bytes;
     bytes += ((size_t)h->N2 * c.emb_dim * 2 + 255) & ~size_t(255);
-    h->xgh_off = bytes;
-    bytes += ((size_t)c.batch * 3 * c.gru_hidden * 2 + 255) & ~size_t(255);
+    h->xgh_off = bytes;  // (mid: N2 >= 2B rows of 2 bytes hold the fp32 [B, E] mid of fp32 heads too)
+    bytes += ((size_t)c.batch * 3 * c.gru_hidden * h->es + 255) & ~size_t(255);
     h->xbuf_bytes = bytes;
   }
   h->max_tiles = ceil_div(c.vocab, kTileM) + ceil_div(c.emb_dim, kTileM) + ceil_div(3LL * c.gru_hidden, kTileM) + 1;
@@ -904,7 +966,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
     return code;
   };
   if (cudaSetDevice(device) != cudaSuccess) return cleanup_fail(fail(nullptr, DD_ECUDA, "cudaSetDevice failed"));
-  const size_t es = 2;
+  const size_t es = h->es;
   const size_t positions = (size_t)npre_max + c.steps;
   struct A {
     void** p;
@@ -933,9 +995,12 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
   }
   h->midbuf = reinterpret_cast<uint8_t*>(h->xbuf) + h->xmid_off;
   h->ghbuf = reinterpret_cast<uint8_t*>(h->xbuf) + h->xgh_off;
-  int rc = encode_kmajor(h, &h->tm_mid, h->midbuf, c.dtype, c.emb_dim, h->N2, c.emb_dim, h->N2);
-  if (!rc) rc = encode_kmajor(h, &h->tm_h[0], h->hbuf[0], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
-  if (!rc) rc = encode_kmajor(h, &h->tm_h[1], h->hbuf[1], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
+  int rc = DD_OK;
+  if (c.dtype != DD_F32) {  // fp32 heads read their operands with plain loads
+    rc = encode_kmajor(h, &h->tm_mid, h->midbuf, c.dtype, c.emb_dim, h->N2, c.emb_dim, h->N2);
+    if (!rc) rc = encode_kmajor(h, &h->tm_h[0], h->hbuf[0], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
+    if (!rc) rc = encode_kmajor(h, &h->tm_h[1], h->hbuf[1], c.dtype, c.gru_hidden, h->N1, c.gru_hidden, h->N1);
+  }
   if (rc) {
     snprintf(g_global_error, sizeof(g_global_error), "%s", h->err);
     return cleanup_fail(rc);
@@ -954,6 +1019,19 @@ int dd_set_weights(dd_handle* h, const dd_weights* w) {
   if (w->table) {
     if (w->table_ld < 3LL * c.gru_hidden || (w->table_ld % 8) != 0 || (reinterpret_cast<uintptr_t>(w->table) & 15))
       return fail(h, DD_EINVAL, "table must be [V, 3G], 16-byte aligned, row stride a multiple of 8 elements");
+  }
+  if (c.dtype == DD_F32) {
+    // fp32 heads: float4 loads of every weight row
+    const void* ptrs[] = {w->fc1, w->fc2, w->w_hh, w->table, w->lm_head};
+    const long long lds[] = {w->fc1_ld, w->fc2_ld, w->w_hh_ld, w->table ? w->table_ld : 0,
+                             w->lm_head ? w->lm_head_ld : 0};
+    for (int i = 0; i < 5; ++i)
+      if ((ptrs[i] && (reinterpret_cast<uintptr_t>(ptrs[i]) & 15)) || (lds[i] & 3))
+        return fail(h, DD_EINVAL, "fp32 weights must be 16-byte aligned with row strides a multiple of 4");
+    if (w->lm_head && w->lm_head_ld < c.hidden) return fail(h, DD_EINVAL, "lm_head_ld smaller than the row length");
+    h->w = *w;
+    h->have_weights = true;
+    return DD_OK;
   }
   const char* esz = reinterpret_cast<const char*>(w->fc1);
   int rc = encode_kmajor(h, &h->tm_wz, w->fc1, c.dtype, c.hidden, c.emb_dim, w->fc1_ld, kTileM);
@@ -1007,9 +1085,15 @@ int dd_build_table(dd_handle* h, const void* embed, int64_t embed_ld, const void
   int rc = use_device(h);
   if (rc) return rc;
   CUtensorMap tm_wih, tm_emb;
-  rc = encode_kmajor(h, &tm_wih, w_ih, c.dtype, c.hidden, 3LL * c.gru_hidden, w_ih_ld, kTileM);
-  if (!rc) rc = encode_kmajor(h, &tm_emb, embed, c.dtype, c.hidden, c.vocab, embed_ld, 256);
-  if (rc) return rc;
+  if (c.dtype == DD_F32) {
+    if ((reinterpret_cast<uintptr_t>(embed) & 15) || (reinterpret_cast<uintptr_t>(w_ih) & 15) || (embed_ld & 3) ||
+        (w_ih_ld & 3))
+      return fail(h, DD_EINVAL, "fp32 embed / w_ih must be 16-byte aligned with row strides a multiple of 4");
+  } else {
+    rc = encode_kmajor(h, &tm_wih, w_ih, c.dtype, c.hidden, 3LL * c.gru_hidden, w_ih_ld, kTileM);
+    if (!rc) rc = encode_kmajor(h, &tm_emb, embed, c.dtype, c.hidden, c.vocab, embed_ld, 256);
+    if (rc) return rc;
+  }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   for (int n_off = 0; n_off < c.vocab; n_off += 256) {
     GemvParams p = base_params(h);
@@ -1022,9 +1106,16 @@ int dd_build_table(dd_handle* h, const void* embed, int64_t embed_ld, const void
     p.table_out = table_out;
     p.table_ld = 3LL * c.gru_hidden;
     p.b_ih = b_ih;
-    rc = c.dtype == DD_FP16
-             ? launch_gemv<__half, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st)
-             : launch_gemv<__nv_bfloat16, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st);
+    p.w32[0] = static_cast<const float*>(w_ih);
+    p.w32_ld[0] = w_ih_ld;
+    p.x32 = static_cast<const float*>(embed);
+    p.x32_ld = embed_ld;
+    if (c.dtype == DD_F32)
+      rc = launch_gemv<float, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st);
+    else if (c.dtype == DD_FP16)
+      rc = launch_gemv<__half, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st);
+    else
+      rc = launch_gemv<__nv_bfloat16, PH_TABLE>(h, tm_wih, nullptr, tm_emb, p, PhaseClass::Big, false, st);
     if (rc) return rc;
   }
   return DD_OK;
@@ -1042,7 +1133,12 @@ int dd_rollout(dd_handle* h, const int64_t* prefix_ids, const void* parallel_hid
   if (rc) return rc;
   // base_logits rows are full-vocab rows; a vocab shard reads its own columns.
   const long long ld = c.vocab, voff = h->v_off;
-  if (c.dtype == DD_FP16) {
+  if (c.dtype == DD_F32) {
+    rc = run_z_phase<float>(h, parallel_hiddens, c.steps, 0, nullptr, st);
+    if (!rc)
+      rc = run_rollout<float>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits, ld, voff,
+                              out_tokens, c.steps, 0, nullptr, st);
+  } else if (c.dtype == DD_FP16) {
     rc = run_z_phase<__half>(h, parallel_hiddens, c.steps, 0, nullptr, st);
     if (!rc)
       rc = run_rollout_persistent<__half>(h, prefix_ids, c.prefix_tokens, c.prefix_tokens, 0, c.steps, base_logits,
@@ -1078,7 +1174,12 @@ int dd_draft_block(dd_handle* h, const int64_t* last_token, const void* parallel
   const int ld = positions + 1;
   // base_logits_out holds this rank's vocab columns only: rows of v_local.
   const long long bld = h->v_local;
-  if (c.dtype == DD_FP16) {
+  if (c.dtype == DD_F32) {
+    rc = run_z_phase<float>(h, parallel_hiddens, positions, npre, base_logits_out, st);
+    if (!rc)
+      rc = run_rollout<float>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out, ld,
+                              1 + npre, verify_out, st);
+  } else if (c.dtype == DD_FP16) {
     rc = run_z_phase<__half>(h, parallel_hiddens, positions, npre, base_logits_out, st);
     if (!rc)
       rc = run_rollout_persistent<__half>(h, last_token, 1, 1, npre, positions, base_logits_out, bld, 0, verify_out,
@@ -1192,6 +1293,7 @@ int dd_set_vocab_shard(dd_handle* h, int32_t rank, int32_t world, int64_t vocab_
     return fail(h, DD_EINVAL, "vocab shard [%lld, %lld) outside [0, %d)", (long long)vocab_begin,
                 (long long)vocab_end, h->cfg.vocab);
   if (world > 1 && !peer_exchange_buffers) return fail(h, DD_EINVAL, "peer exchange buffers are required");
+  if (world > 1 && h->cfg.dtype == DD_F32) return fail(h, DD_EUNSUPPORTED, "vocab sharding needs bf16 / fp16 weights");
   for (int j = 0; j < kMaxRanks; ++j) h->peer[j] = nullptr;
   for (int j = 0; j < world; ++j) {
     void* pj = (world == 1 || j == rank) ? h->xbuf : peer_exchange_buffers[j];
@@ -1339,7 +1441,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   const dd_config& c = *cfg;
   if (c.batch < 1 || c.batch > kMaxBatch || c.steps < 1 || c.hidden < 8 || c.gru_hidden < 8 || c.emb_dim < 8 ||
       c.vocab < 2 || c.prefix_tokens < 1 || c.hidden % 8 || c.gru_hidden % 8 || c.emb_dim % 8 ||
-      (c.dtype != DD_BF16 && c.dtype != DD_FP16))
+      (c.dtype != DD_BF16 && c.dtype != DD_FP16 && c.dtype != DD_F32))
     return fail(nullptr, DD_EINVAL, "dd_rollout_noalloc: bad config (same rules as dd_create)");
 
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
@@ -1376,6 +1478,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.err[0] = 0;
   h.N1 = round_up(c.batch, 16);
   h.N2 = round_up(2 * c.batch, 16);
+  h.es = c.dtype == DD_F32 ? 4 : 2;
   h.v_off = 0;
   h.v_local = c.vocab;  // unsharded
   h.world = 1;
@@ -1399,11 +1502,12 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
     return p;
   };
   h.status = reinterpret_cast<unsigned int*>(d.base);
-  h.zbuf = take((size_t)c.batch * positions * c.emb_dim * 2);
-  h.midbuf = take((size_t)h.N2 * c.emb_dim * 2);
-  h.hbuf[0] = take((size_t)h.N1 * c.gru_hidden * 2);
-  h.hbuf[1] = take((size_t)h.N1 * c.gru_hidden * 2);
-  h.ghbuf = take((size_t)c.batch * 3 * c.gru_hidden * 2);
+  const size_t es = h.es;
+  h.zbuf = take((size_t)c.batch * positions * c.emb_dim * es);
+  h.midbuf = take((size_t)h.N2 * c.emb_dim * 2);  // N2 >= 2B rows: also holds fp32 [B, E]
+  h.hbuf[0] = take((size_t)h.N1 * c.gru_hidden * es);
+  h.hbuf[1] = take((size_t)h.N1 * c.gru_hidden * es);
+  h.ghbuf = take((size_t)c.batch * 3 * c.gru_hidden * es);
   h.slots = reinterpret_cast<unsigned long long*>(take((size_t)c.batch * h.nslots * 8));
   h.partials = reinterpret_cast<float*>(take((size_t)2 * h.max_ctas * n_part * kTileM * 4));
   h.counters = reinterpret_cast<unsigned int*>(take((size_t)h.max_tiles * 4));
@@ -1422,16 +1526,19 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
     void* p;
     size_t n;
   } zero[] = {{h.midbuf, (size_t)h.N2 * c.emb_dim * 2},
-              {h.hbuf[0], (size_t)h.N1 * c.gru_hidden * 2},
-              {h.hbuf[1], (size_t)h.N1 * c.gru_hidden * 2},
+              {h.hbuf[0], (size_t)h.N1 * c.gru_hidden * es},
+              {h.hbuf[1], (size_t)h.N1 * c.gru_hidden * es},
               {h.counters, (size_t)h.max_tiles * 4}};
   for (const auto& z : zero)
     if (cudaMemsetAsync(z.p, 0, z.n, st) != cudaSuccess)
       return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cudaMemsetAsync failed");
 
-  int rc = encode_kmajor(&h, &h.tm_mid, h.midbuf, c.dtype, c.emb_dim, h.N2, c.emb_dim, h.N2);
-  if (!rc) rc = encode_kmajor(&h, &h.tm_h[0], h.hbuf[0], c.dtype, c.gru_hidden, h.N1, c.gru_hidden, h.N1);
-  if (!rc) rc = encode_kmajor(&h, &h.tm_h[1], h.hbuf[1], c.dtype, c.gru_hidden, h.N1, c.gru_hidden, h.N1);
+  int rc = DD_OK;
+  if (c.dtype != DD_F32) {
+    rc = encode_kmajor(&h, &h.tm_mid, h.midbuf, c.dtype, c.emb_dim, h.N2, c.emb_dim, h.N2);
+    if (!rc) rc = encode_kmajor(&h, &h.tm_h[0], h.hbuf[0], c.dtype, c.gru_hidden, h.N1, c.gru_hidden, h.N1);
+    if (!rc) rc = encode_kmajor(&h, &h.tm_h[1], h.hbuf[1], c.dtype, c.gru_hidden, h.N1, c.gru_hidden, h.N1);
+  }
   if (!rc) rc = dd_set_weights(&h, w);
   if (!rc) rc = dd_rollout(&h, prefix_ids, parallel_hiddens, base_logits, out_tokens, stream);
   return rc ? noalloc_fail(&h, rc) : DD_OK;

@@ -58,10 +58,14 @@ __device__ __forceinline__ unsigned long long gathered_word(const CellParams& p,
   return best;
 }
 
+// Eight consecutive elements (16 bytes for 2-byte types, 32 for fp32; aligned).
 template <typename T>
 __device__ __forceinline__ void load8(const T* p, float (&f)[8]) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
-  const T* e = reinterpret_cast<const T*>(&raw);
+  constexpr int kVecs = (int)sizeof(T) * 8 / 16;
+  uint4 raw[kVecs];
+#pragma unroll
+  for (int v = 0; v < kVecs; ++v) raw[v] = reinterpret_cast<const uint4*>(p)[v];
+  const T* e = reinterpret_cast<const T*>(raw);
 #pragma unroll
   for (int i = 0; i < 8; ++i) f[i] = io<T>::to_f(e[i]);
 }
@@ -127,8 +131,11 @@ __device__ __forceinline__ void cell_apply(const CellParams& p, int idx) {
     const float n = 2.0f * sigmoidf_(2.0f * (in_[i] + r * hn[i])) - 1.0f;
     outv[i] = io<T>::from_f((1.0f - z) * n + z * h[i]);
   }
-  *reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h_out) + (size_t)b * G + g0) =
-      *reinterpret_cast<const uint4*>(outv);
+  constexpr int kVecs = (int)sizeof(T) * 8 / 16;
+#pragma unroll
+  for (int v = 0; v < kVecs; ++v)
+    reinterpret_cast<uint4*>(reinterpret_cast<T*>(p.h_out) + (size_t)b * G + g0)[v] =
+        reinterpret_cast<const uint4*>(outv)[v];
 }
 
 template <typename T>

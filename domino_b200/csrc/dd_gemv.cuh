@@ -157,6 +157,12 @@ struct GemvParams {
   Exchange xchg;
   int xslot0, xslot1;  // argmax words this launch publishes to every rank
   int sflag_slot;      // >= 0: this s / gh launch raises its step flag on every rank when done
+  // fp32 heads (gemv_f32_kernel): the segments' weights and the X rows as
+  // plain pointers, row strides in elements.
+  const float* w32[2];
+  long long w32_ld[2];
+  const float* x32;
+  long long x32_ld;
 };
 
 // CTA c's units are [unit_begin(c), unit_begin(c + 1)): equal contiguous

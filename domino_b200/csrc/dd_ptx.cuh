@@ -230,6 +230,13 @@ struct io<__half> {
   static __device__ __forceinline__ __half from_f(float v) { return __float2half_rn(v); }
 };
 
+template <>
+struct io<float> {
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+
 // Logistic in fp32 from expf, the form 1 / (1 + exp(-x)).
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 

@@ -59,7 +59,7 @@ def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
-_DTYPES = {torch.bfloat16: _lib.DD_BF16, torch.float16: _lib.DD_FP16}
+_DTYPES = {torch.bfloat16: _lib.DD_BF16, torch.float16: _lib.DD_FP16, torch.float32: _lib.DD_F32}
 
 
 class DraftCorrectionGraphRunner:
@@ -120,7 +120,7 @@ class DraftCorrectionGraphRunner:
 
         dtype = next(draft_model.parameters()).dtype
         if dtype not in _DTYPES:
-            raise NotImplementedError(f"the B200 runner computes in bf16/fp16 weights, got {dtype}")
+            raise NotImplementedError(f"the B200 runner computes with bf16, fp16 or fp32 weights, got {dtype}")
         self.dtype = dtype
         device = torch.device(device)
         if device.type != "cuda":

@@ -84,7 +84,7 @@ def test_runner_validates_like_the_reference():
     with pytest.raises(NotImplementedError):
         _mk(nn.Sequential(nn.Linear(16, 12), nn.GELU(), nn.Linear(12, 10)))
     with pytest.raises(NotImplementedError):
-        _mk(nn.Sequential(nn.Linear(16, 12), nn.SiLU(), nn.Linear(12, 10)), dtype=torch.float32)
+        _mk(nn.Sequential(nn.Linear(16, 12), nn.SiLU(), nn.Linear(12, 10)), dtype=torch.float64)
     with pytest.raises(ValueError):
         _mk(nn.Sequential(nn.Linear(16, 12), nn.SiLU(), nn.Linear(12, 10)),
             gru=nn.GRU(8, 8, num_layers=2, batch_first=True))

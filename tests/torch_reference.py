@@ -11,8 +11,11 @@ from __future__ import annotations
 import torch
 
 
+_ROUND = [True]  # False: fp32 heads, nothing is rounded (set by teacher_forced_rollout)
+
+
 def _rb(x: torch.Tensor) -> torch.Tensor:
-    return x.to(torch.bfloat16).float()
+    return x.to(torch.bfloat16).float() if _ROUND[0] else x.float()
 
 
 def _linear(x, w, b=None):
@@ -30,6 +33,7 @@ def _cell(gi, gh, h):
     return _rb((1.0 - z) * n + z * h)
 
 
+@torch.no_grad()
 def build_table(embed, w_ih, b_ih=None):
     """The GRU input table ``F.linear(embed, W_ih, b_ih)`` (code/kernel/domino.py:322-327),
     computed here by cuBLAS in the weight dtype, independently of the kernel under test."""
@@ -38,7 +42,7 @@ def build_table(embed, w_ih, b_ih=None):
 
 @torch.no_grad()
 def teacher_forced_rollout(fc1, fc2, w_hh, table, prefix_ids, parallel_hiddens, base_logits, tokens,
-                           fc1_bias=None, fc2_bias=None, b_hh=None, states=None):
+                           fc1_bias=None, fc2_bias=None, b_hh=None, states=None, round_bf16=True):
     """Own argmax, logit of the fed token and top logit per step, fed ``tokens``.
 
     fc1 [E, H+G], fc2 [V, E], w_hh [3G, G], table [V, 3G] (bf16 tensors on the
@@ -46,8 +50,10 @@ def teacher_forced_rollout(fc1, fc2, w_hh, table, prefix_ids, parallel_hiddens, 
     tokens [B, S] (the tokens under test).  With ``states`` (a dict) it also
     records the per-step states in the layout of the runner's ``rollout_trace``:
     ``z`` [B, S, E], ``h`` [P + S - 1, B, G], ``gh`` [P + S - 2, B, 3G],
-    ``s`` [S, B, E] (fp32 tensors holding bf16-rounded values).
+    ``s`` [S, B, E] (fp32 tensors holding bf16-rounded values).  With
+    ``round_bf16=False`` nothing is rounded (fp32 heads).
     """
+    _ROUND[0] = round_bf16
     B, S, H = parallel_hiddens.shape
     G = w_hh.shape[1]
     P = prefix_ids.shape[1]
