@@ -123,6 +123,7 @@ struct dd_handle {
   unsigned int* rbar = nullptr;
   int rollout_mode = 1;
   int min_units_per_cta = 8;
+  int l2_prefetch_kb = 0;  // DD_L2_PREFETCH_KB: weight bytes per CTA prefetched into L2 past the ring
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
@@ -260,6 +261,7 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   const uint32_t ring_budget =
       p.N > 64 ? 196u * 1024u : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
   p.stages = std::max(4, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  p.l2_prefetch_units = (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
   p.xpose_bytes = (kPhase == PH_ZLM || kPhase == PH_Z || kPhase == PH_TABLE) ? kXposeBytes : 0u;
   const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes;
   if ((size_t)p.stages * p.stage_bytes + fixed > 227 * 1024) p.stages = (227 * 1024 - fixed) / p.stage_bytes;
@@ -882,7 +884,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
-// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS) over the defaults of a fresh
+// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -903,6 +905,7 @@ void read_launch_env(dd_handle* h) {
   h->min_units_per_cta = env_int("DD_MIN_UNITS_PER_CTA", d.min_units_per_cta, 1, 64);
   h->max_nacc = env_int("DD_NACC", d.max_nacc, 1, 4);
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", d.tmem_cols_per_cta, 32, 512);
+  h->l2_prefetch_kb = env_int("DD_L2_PREFETCH_KB", d.l2_prefetch_kb, 0, 4096);
 }
 
 }  // namespace

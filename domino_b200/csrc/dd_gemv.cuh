@@ -113,6 +113,7 @@ struct GemvParams {
   int n_valid;       // X rows of this pass that carry data (<= N)
   long long units;   // (tile, k-chunk) units in this pass
   int stages;
+  int l2_prefetch_units;  // weight tiles past the ring this CTA prefetches into L2 before waiting on its predecessor
   uint32_t stage_bytes;
   uint32_t b_bytes;
   int acc_slots;
@@ -752,6 +753,28 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (++kc == KC) {
           kc = 0;
           ++tile;
+        }
+      }
+      // Then the weight tiles after the ring into L2: while this kernel waits
+      // for the one before it (which may be latency-bound: a short launch, a
+      // tail, the GRU cell), HBM keeps streaming this phase's weights.
+      {
+        const long long npf = n_my - pre < p.l2_prefetch_units ? n_my - pre : p.l2_prefetch_units;
+        long long pt = tile;
+        int pk = kc;
+        for (long long i = 0; i < npf; ++i) {
+          const bool s1 = pt >= p.seg[0].tiles;
+          const GemvSeg& sg = p.seg[s1 ? 1 : 0];
+          const long long w_tile = (s1 ? pt - p.seg[0].tiles : pt) + sg.row_off / kTileM;
+          const uint8_t* pk_base = p.packed[s1 ? 1 : 0];
+          if (pk_base)
+            bulk_prefetch_l2(pk_base + (size_t)(w_tile * KC + pk) * kATileBytes, kATileBytes);
+          else
+            tma_prefetch_l2_2d(s1 ? &tmA1 : &tmA0, pk * kChunkK, (int)(w_tile * kTileM));
+          if (++pk == KC) {
+            pk = 0;
+            ++pt;
+          }
         }
       }
       pdl_wait_primary();

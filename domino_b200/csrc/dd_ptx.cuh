@@ -112,6 +112,21 @@ __device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint3
       : "memory");
 }
 
+// Prefetch the box at (c0, c1) of a tensor map into L2: no shared memory, no
+// barrier; a later TMA load of the same box then reads it from L2.
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* m, int32_t c0, int32_t c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
+               "r"(c0), "r"(c1)
+               : "memory");
+}
+
+// Prefetch `bytes` contiguous global bytes into L2 (16-byte aligned, size a
+// multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }

@@ -123,7 +123,7 @@ def random_inputs(B, S, H, V, P, target, *, seed=0, device="cuda", dtype=torch.b
     return prefix, ph, base
 
 
-def teacher_forced_check(w: O.DraftWeights, prefix, ph, base, gpu_tokens, min_exact=0.9):
+def teacher_forced_check(w: O.DraftWeights, prefix, ph, base, gpu_tokens, min_exact=1.0):
     """Every GPU token equals the oracle's argmax given the same history, or is
     within TOL of the oracle's top logit (a near-tie).  Returns the exact-match
     fraction; asserts it is at least ``min_exact``."""

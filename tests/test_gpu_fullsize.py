@@ -105,9 +105,8 @@ def test_fullsize_draft_block_and_accept(model):
     assert runner.status() == 0
     ref = base.float()
     assert torch.all((base_out.float() - ref).abs() <= TOL + TOL * ref.abs())
-    # identical base logits -> identical tokens to the runner call
-    out = runner(prefix, ph, base_out)
-    assert torch.equal(verify[:, 1:], out)
+    # the fused block's tokens pass the teacher-forced check on its own base logits
+    check_tokens_and_states(draft, target, runner, prefix, ph, base_out, verify[:, 1:])
     # a target that agrees with the draft accepts the whole block
     posterior = torch.cat([verify[:, 1:], verify[:, -1:]], 1)
     acc, bonus = runner.accept(verify, posterior)
@@ -147,12 +146,17 @@ def test_fullsize_batch_states_and_fused_block(B, Hc, Ec):
         # (first run on B200: 479 of 480 exact, slack 0.0044).
         check_tokens_and_states(draft, target, runner, prefix, ph, base, out, states, min_exact=0.99)
         # The fused block: lm_head over B * 15 rows (two MMA passes at B = 32)
-        # gives cuBLAS's base logits, and then the runner's tokens.
+        # gives cuBLAS's base logits, and its tokens pass the same
+        # teacher-forced check.  (Its z projection shares a launch with
+        # lm_head, so its fp32 partial sums split at other k than the plain
+        # runner call's: z can differ by a bf16 ulp and flip a near-tie.)
         verify, base_out = runner.draft_block(prefix[:, 0], ph)
         assert runner.status() == 0
         mx, same = compare_states("base logits", base_out, base)
-        log_parity(f"fused lm_head base logits max|d| {mx:.3g} bit-equal {same:.4f}")
-        assert torch.equal(verify[:, 1:], runner(prefix, ph, base_out))
+        plain = runner(prefix, ph, base_out)
+        log_parity(f"fused lm_head base logits max|d| {mx:.3g} bit-equal {same:.4f}; block tokens equal to the "
+                   f"runner call's: {int((verify[:, 1:] == plain).sum())}/{plain.numel()}")
+        check_tokens_and_states(draft, target, runner, prefix, ph, base_out, verify[:, 1:], min_exact=0.99)
     finally:
         runner.close()
         del runner, draft, target

@@ -189,10 +189,14 @@ def test_vocab_shard_two_gpus_matches_unsharded():
     # every rank produced the same tokens
     assert np.array_equal(res[0]["outs"][0], res[1]["outs"][0])
     assert np.array_equal(res[0]["verify"], res[1]["verify"])
-    from tests.gpu_helpers import teacher_forced_check
+    from tests.gpu_helpers import log_parity, teacher_forced_check
 
     prefix, ph, base = res[0]["inputs"]
-    teacher_forced_check(res[0]["w"], prefix, ph, base, res[0]["outs"][0])
+    # the shards split the fp32 sums at other points than one GPU does, so a
+    # near-tie may go either way
+    teacher_forced_check(res[0]["w"], prefix, ph, base, res[0]["outs"][0], min_exact=0.95)
     # equal to the unsharded runner except at near-ties
-    assert float(np.mean(res[0]["outs"][0] != res[0]["ref"])) <= 0.1
+    differ = float(np.mean(res[0]["outs"][0] != res[0]["ref"]))
+    log_parity(f"2-GPU vocab shard: {1 - differ:.3f} of the tokens equal the unsharded runner's")
+    assert differ <= 0.1
     assert np.array_equal(res[0]["verify"][:, 0], prefix[:, 0])
