@@ -70,6 +70,13 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=150.0)
+    ap.add_argument("--spec-loop", action="store_true",
+                    help="the end-to-end synthetic spec-decode loop instead of the draft step: a random-init "
+                         "Qwen3-8B-shaped target (36 layers) verifying the drafter's blocks")
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--new-tokens", type=int, default=2048)
+    ap.add_argument("--draft-layers", type=int, default=5)
+    ap.add_argument("--requests", type=int, default=2, help="--spec-loop: requests per GPU")
     return ap.parse_args()
 
 
@@ -572,9 +579,117 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- end-to-end loop
+def _random_stack(cls, cfg, device, seed):
+    """A stack module built on the device in bf16 with seeded N(0, 0.02) weights (norms 1)."""
+    import torch
+
+    prev = torch.get_default_dtype()
+    torch.set_default_dtype(torch.bfloat16)
+    try:
+        with torch.device(device):
+            m = cls(cfg)
+    finally:
+        torch.set_default_dtype(prev)
+    g = torch.Generator(device=device).manual_seed(seed)
+    with torch.no_grad():
+        for name, p in m.named_parameters():
+            if name.endswith("norm.weight"):
+                p.fill_(1.0)
+            else:
+                p.normal_(0.0, 0.02, generator=g)
+    return m.eval()
+
+
+def run_spec_loop(args):
+    """The end-to-end synthetic spec-decode workload: per GPU, ``--requests``
+    requests (default 2) of ``--prompt-len`` random ids, ``--new-tokens``
+    greedy tokens in blocks of 16, a random-init Qwen3-8B-shaped target (36
+    layers, H 4096, 32 q / 8 kv heads) verifying a DFlash drafter with the
+    Qwen3-8B-shaped Domino head.  One process per GPU, each with its own
+    requests (weak scaling); times are CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from domino_b200 import DraftCorrectionGraphRunner
+    from domino_b200.parallel import max_over_ranks
+    from domino_b200.spec_decode import spec_generate
+    from domino_b200.stack import DFlashBackbone, StackConfig, TargetLM, build_target_layer_ids
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", init_method="env://", timeout=datetime.timedelta(seconds=600),
+                                device_id=device)
+    H, G, E, V, S, P = shapes(args)
+    B = args.requests
+    tcfg = StackConfig(vocab_size=V, hidden_size=H, intermediate_size=3 * H, num_hidden_layers=36,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=H // 32, rope_theta=1e6)
+    dcfg = StackConfig(vocab_size=V, hidden_size=H, intermediate_size=3 * H, num_hidden_layers=args.draft_layers,
+                       num_attention_heads=32, num_key_value_heads=8, head_dim=H // 32, rope_theta=1e6,
+                       block_size=args.block, target_layer_ids=build_target_layer_ids(36, args.draft_layers),
+                       mask_token_id=V - 1, emb_dim=E, gru_hidden_dim=G, pure_draft_prefix_len=P)
+    target = _random_stack(TargetLM, tcfg, device, args.seed)
+    draft = _random_stack(DFlashBackbone, dcfg, device, args.seed + 1)
+    runner = DraftCorrectionGraphRunner(draft, target, B, S, H, G, V, P + 1, device, use_graph=False)
+    g = torch.Generator().manual_seed(args.seed + 100 + rank)
+    prompts = [torch.randint(0, V - 1, (args.prompt_len,), generator=g) for _ in range(B)]
+    spec_generate(draft, target, runner, prompts, 64)  # warm-up
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    if rank == 0:
+        clocks.start()
+    res = spec_generate(draft, target, runner, prompts, args.new_tokens, time_blocks=True)
+    clk = clocks.stop() if rank == 0 else None
+    status = runner.status()
+    drafted = res.blocks * B * S
+    generated = sum(res.num_output_tokens)
+    decode_ms, draft_ms, verify_ms, status_f = max_over_ranks([res.decode_ms, res.draft_ms, res.verify_ms,
+                                                               float(status)], device=device)
+    sums = torch.tensor([drafted, generated, res.blocks], dtype=torch.float64, device=device)
+    hist = torch.zeros(args.block + 2, dtype=torch.float64, device=device)
+    for accs in res.acceptance_lengths:
+        for a in accs:
+            hist[min(a, args.block + 1)] += 1
+    if world > 1:
+        dist.all_reduce(sums)
+        dist.all_reduce(hist)
+    if rank == 0:
+        drafted_all, generated_all, blocks_all = (float(x) for x in sums.tolist())
+        line = {
+            "metric": "end-to-end spec decode: draft tokens/s and generated tokens/s (CUDA events)",
+            "value": round(drafted_all / (draft_ms / 1e3), 2), "unit": "draft tokens/s",
+            "generated_tokens_per_s": round(generated_all / (decode_ms / 1e3), 2),
+            "n_gpus": world, "requests_per_gpu": B, "higher_is_better": True, "scaling": "weak",
+            "dtype": "bf16", "data": "synthetic: random-init Qwen3-8B-shaped target and drafter, random prompt ids",
+            "config": {"workload": f"spec decode, {B} requests/GPU, prompt {args.prompt_len}, {args.new_tokens} new "
+                                   f"tokens, block {args.block}; target Qwen3-8B-shaped (36 layers, H={H}, 32 q / 8 "
+                                   f"kv heads); drafter {args.draft_layers} DFlash layers + Domino head (E={E}, G={G})",
+                       "parallelism": f"dp{world} (requests sharded, no collective)"},
+            "decode_ms": round(decode_ms, 1), "draft_ms": round(draft_ms, 1), "verify_ms": round(verify_ms, 1),
+            "blocks_per_gpu": res.blocks,
+            "ms_per_block": round(decode_ms / res.blocks, 3),
+            "draft_ms_per_block": round(draft_ms / res.blocks, 3),
+            "verify_ms_per_block": round(verify_ms / res.blocks, 3),
+            "accept_len_hist": [int(x) for x in hist.tolist()],
+            "mean_accept_len": round(sum(i * x for i, x in enumerate(hist.tolist())) / max(1.0, sum(hist.tolist())), 4),
+            "device_status": int(status_f), "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    runner.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.spec_loop:
+        run_spec_loop(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -35,3 +35,32 @@ def weights(fx: dict, dtype: str | None = None) -> DraftWeights:
 
 ROLLOUT_CASES = ["rollout_bf16_b1", "rollout_bf16_b3_bias", "rollout_fp32_b1"]
 TRACE_CASES = ["spec_trace_random", "spec_trace_full_accept", "spec_trace_partial"]
+
+
+LOOP_CASES = ["spec_loop_random", "spec_loop_varied", "spec_loop_full"]
+
+
+def load_loop(name: str, device="cpu"):
+    """A spec_generate fixture (tests/golden/make_golden.py spec_loop_case):
+    the tiny target and drafter with the reference's weights, the prompts, and
+    the reference's output ids and acceptance lengths per prompt."""
+    import json
+
+    import torch
+
+    from domino_b200.stack import DFlashBackbone, StackConfig, TargetLM
+
+    fx = load(name)
+    tcfg = StackConfig(**json.loads(str(fx["target_config"])))
+    dcfg = StackConfig(**json.loads(str(fx["draft_config"])))
+    target, draft = TargetLM(tcfg), DFlashBackbone(dcfg)
+    target.load_state_dict({k[2:]: torch.from_numpy(v) for k, v in fx.items() if k.startswith("t.")}, strict=True)
+    draft.load_state_dict({k[2:]: torch.from_numpy(v) for k, v in fx.items() if k.startswith("d.")}, strict=True)
+    n = int(fx["n_prompts"])
+    return dict(
+        target=target.to(device).eval(), draft=draft.to(device).eval(), fx=fx,
+        prompts=[torch.from_numpy(fx[f"prompt_{i}"]) for i in range(n)],
+        outputs=[fx[f"output_{i}"] for i in range(n)],
+        accepts=[fx[f"accept_{i}"].tolist() for i in range(n)],
+        max_new_tokens=int(fx["max_new_tokens"]),
+    )

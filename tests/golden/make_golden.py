@@ -320,6 +320,103 @@ def spec_generate_trace(name, *, seed, mode: str, max_new_tokens: int):
     print(f"{name}: {n} blocks, acceptance lengths {res.acceptance_lengths}")
 
 
+def _config_json(cfg) -> str:
+    """The Qwen3 config fields a Qwen3-style stack needs, as JSON."""
+    import json
+
+    rope = getattr(cfg, "rope_parameters", None) or {}
+    d = dict(vocab_size=cfg.vocab_size, hidden_size=cfg.hidden_size, intermediate_size=cfg.intermediate_size,
+             num_hidden_layers=cfg.num_hidden_layers, num_attention_heads=cfg.num_attention_heads,
+             num_key_value_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, rms_norm_eps=cfg.rms_norm_eps,
+             rope_theta=float(rope.get("rope_theta", getattr(cfg, "rope_theta", 10000.0))))
+    dc = getattr(cfg, "dflash_config", None)
+    if dc:
+        d.update(block_size=cfg.block_size, target_layer_ids=list(dc["target_layer_ids"]),
+                 mask_token_id=dc["mask_token_id"], emb_dim=dc["emb_dim"], gru_hidden_dim=dc["gru_hidden_dim"],
+                 pure_draft_prefix_len=dc.get("pure_draft_prefix_len", 0))
+    return json.dumps(d)
+
+
+def spec_loop_case(name, *, seed, mode: str, prompt_lens, max_new_tokens: int, draft_layers: int = 1,
+                   target_layer_ids=(1,), prefix_len: int = 0):
+    """The reference's whole spec_generate (code/dflash.py:304-526) for several
+    prompts, one call each (it is batch-1 only), with every parameter of the
+    tiny target and drafter saved so that another implementation of the loop
+    can be checked against its outputs and acceptance lengths.
+
+    Modes as in spec_generate_trace: "random" heads (acceptance mostly 1);
+    "partial" (zero target logits, one live fc2 row); "full" (every draft
+    token accepted); "varied" (see below: acceptance varies per block and per
+    prompt).
+    """
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from dflash import DFlashDraftModel
+
+    torch.manual_seed(seed)
+    H, V, E, G = 64, 600, 96, 64
+    tcfg = Qwen3Config(
+        vocab_size=V, hidden_size=H, intermediate_size=128, num_hidden_layers=4,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=512,
+    )
+    tcfg._attn_implementation = "eager"
+    target = Qwen3ForCausalLM(tcfg).eval()
+    dcfg = Qwen3Config(
+        vocab_size=V, hidden_size=H, intermediate_size=128, num_hidden_layers=draft_layers,
+        num_attention_heads=4, num_key_value_heads=2, head_dim=16, max_position_embeddings=512,
+    )
+    dcfg._attn_implementation = "eager"
+    dcfg.block_size = 16
+    dcfg.num_target_layers = 4
+    dcfg.dflash_config = {
+        "projector_type": "domino", "emb_dim": E, "gru_hidden_dim": G, "mask_token_id": V - 1,
+        "pure_draft_prefix_len": prefix_len, "target_layer_ids": list(target_layer_ids),
+    }
+    draft = DFlashDraftModel(dcfg).eval()
+    with torch.no_grad():
+        for p in draft.embed_proj.parameters():
+            p.normal_(0.0, 0.02)
+        for p in draft.prefix_gru.parameters():
+            p.normal_(0.0, 0.05)
+        if mode in ("full", "partial"):
+            target.model.norm.weight.zero_()
+            draft.norm.weight.zero_()
+            draft.embed_proj[2].weight.zero_()
+        if mode == "partial":
+            draft.embed_proj[2].weight[5].normal_(0.0, 0.5)
+        if mode == "varied":
+            # zero target lm_head: posterior 0 everywhere and base logits 0;
+            # the drafter's hidden states stay live, so the sign of token 5's
+            # correction (the one live fc2 row) changes from position to
+            # position and row to row, and so does the acceptance
+            target.lm_head.weight.zero_()
+            draft.embed_proj[2].weight.zero_()
+            row = torch.randn(E) * 0.5
+            draft.embed_proj[2].weight[5] = row - row.mean()  # zero-mean: the sign follows mid's fluctuations
+            draft.embed_proj[0].weight[:, :H] *= 20.0  # a large z part: mid moves with the block's hidden states
+    kd.HAS_TRITON = True
+    S = 15 - prefix_len
+    runner = kd.DraftCorrectionGraphRunner(draft, target, 1, S, H, G, V, 1 + prefix_len, torch.device("cpu"))
+    runner.graph.fn = runner._forward_impl
+    data = {"target_config": np.array(_config_json(tcfg)), "draft_config": np.array(_config_json(dcfg)),
+            "max_new_tokens": np.array(max_new_tokens)}
+    for k, v in target.state_dict().items():
+        data["t." + k] = v.detach().numpy()
+    for k, v in draft.state_dict().items():
+        data["d." + k] = v.detach().numpy()
+    accs = []
+    for i, n in enumerate(prompt_lens):
+        prompt = torch.randint(0, V - 1, (1, n))
+        res = draft.spec_generate(prompt, target, max_new_tokens=max_new_tokens, temperature=0.0, block_size=16,
+                                  graph_runner=runner, return_dict=True)
+        data[f"prompt_{i}"] = prompt[0].numpy()
+        data[f"output_{i}"] = res.output_ids[0].numpy()
+        data[f"accept_{i}"] = np.array(res.acceptance_lengths, np.int64)
+        accs.append(res.acceptance_lengths)
+    data["n_prompts"] = np.array(len(prompt_lens))
+    np.savez_compressed(OUT / f"{name}.npz", **data)
+    print(f"{name}: acceptance lengths per prompt {accs}")
+
+
 def main():
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     with torch.inference_mode():
@@ -331,6 +428,11 @@ def main():
     spec_generate_trace("spec_trace_random", seed=4, mode="random", max_new_tokens=10)
     spec_generate_trace("spec_trace_full_accept", seed=5, mode="full", max_new_tokens=40)
     spec_generate_trace("spec_trace_partial", seed=38, mode="partial", max_new_tokens=20)
+    loops = dict(prompt_lens=(24, 13, 31))
+    spec_loop_case("spec_loop_random", seed=6, mode="random", max_new_tokens=24, draft_layers=2,
+                   target_layer_ids=(1, 2), prefix_len=1, **loops)
+    spec_loop_case("spec_loop_varied", seed=38, mode="varied", max_new_tokens=48, **loops)
+    spec_loop_case("spec_loop_full", seed=5, mode="full", max_new_tokens=40, **loops)
 
 
 if __name__ == "__main__":
