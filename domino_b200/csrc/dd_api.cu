@@ -124,6 +124,8 @@ struct dd_handle {
   int rollout_mode = 1;
   int min_units_per_cta = 8;
   int l2_prefetch_kb = 0;  // DD_L2_PREFETCH_KB: weight bytes per CTA prefetched into L2 past the ring
+  int fuse_cell = 1;       // DD_FUSE_CELL: the GRU cell runs in the fc2 launch's tail
+  unsigned int* gbar = nullptr;  // grid barrier of the fused cell: [0] count, [1] generation
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
@@ -348,8 +350,8 @@ int launch_gemv(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, cons
 
 Exchange make_exchange(const dd_handle* h);
 
-template <typename T>
-int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
+// The handle-wide fields of a GRU step.
+void fill_cell(const dd_handle* h, CellParams& cp) {
   cp.B = h->cfg.batch;
   cp.G = h->cfg.gru_hidden;
   cp.V = h->cfg.vocab;
@@ -359,6 +361,11 @@ int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
   cp.status = h->status;
   cp.xchg = make_exchange(h);
   cp.xbuf = h->xbuf;
+}
+
+template <typename T>
+int launch_cell(dd_handle* h, CellParams cp, cudaStream_t st) {
+  fill_cell(h, cp);
   const int threads = cp.B * (cp.G / 8);
   int rc = timing_begin(h, DD_PHASE_CELL, st);
   if (rc) return rc;
@@ -646,10 +653,6 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       p.w32_ld[0] = h->w.fc2_ld;
       p.x32 = static_cast<const float*>(h->midbuf);  // fp32 heads: mid is [B, E] fp32
       p.x32_ld = c.emb_dim;
-      rc = launch_gemv<T, PH_FC2>(h, h->tm_fc2, nullptr, h->tm_mid, p, PhaseClass::Big, true, st);
-      if (rc) return rc;
-    }
-    {
       CellParams cp;
       memset(&cp, 0, sizeof(cp));
       cp.src = 1;
@@ -663,7 +666,17 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       cp.gh = h->ghbuf;
       cp.h_in = h->hbuf[cur];
       cp.h_out = h->hbuf[cur ^ 1];
-      rc = launch_cell<T>(h, cp, st);
+      // The step's GRU cell runs in the fc2 launch itself (after a grid-wide
+      // barrier) on unsharded bf16 / fp16 handles; a launch of its own otherwise.
+      const bool fuse = h->fuse_cell && h->world == 1 && !h->tracing && !std::is_same<T, float>::value;
+      if (fuse) {
+        fill_cell(h, cp);
+        p.fused_cell = 1;
+        p.gbar = h->gbar;
+        p.cell = cp;
+      }
+      rc = launch_gemv<T, PH_FC2>(h, h->tm_fc2, nullptr, h->tm_mid, p, PhaseClass::Big, true, st);
+      if (!rc && !fuse) rc = launch_cell<T>(h, cp, st);
       if (!rc && !last) rc = trace_copy(h, h->trace.h, n_prefix_total + t, h->hbuf[cur ^ 1], c.batch, c.gru_hidden, st);
       if (rc) return rc;
       cur ^= 1;
@@ -884,7 +897,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
-// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB) over the defaults of a fresh
+// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -906,6 +919,7 @@ void read_launch_env(dd_handle* h) {
   h->max_nacc = env_int("DD_NACC", d.max_nacc, 1, 4);
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", d.tmem_cols_per_cta, 32, 512);
   h->l2_prefetch_kb = env_int("DD_L2_PREFETCH_KB", d.l2_prefetch_kb, 0, 4096);
+  h->fuse_cell = env_int("DD_FUSE_CELL", d.fuse_cell, 0, 1);
 }
 
 }  // namespace
@@ -989,6 +1003,7 @@ int dd_create(const dd_config* cfg, int device, dd_handle** out) {
       {(void**)&h->vwords, (size_t)c.batch * dd_handle::kMaxVerifyPositions * 8},
       {(void**)&h->vdone, 64},
       {(void**)&h->rbar, (size_t)(kMaxRollPhases + 1) * 4},
+      {(void**)&h->gbar, 64},
   };
   for (auto& a : allocs) {
     if (cudaMalloc(a.p, a.bytes) != cudaSuccess)
@@ -1383,8 +1398,8 @@ int dd_destroy(dd_handle* h) {
   cudaGetDevice(&prev);
   cudaSetDevice(h->device);
   // (midbuf and ghbuf live inside xbuf)
-  void* ptrs[] = {h->zbuf, h->hbuf[0], h->hbuf[1], h->slots,  h->partials, h->counters, h->status,
-                  h->xbuf, h->xseq,    h->xdone,   h->xsdone, h->vwords,   h->vdone,    h->rbar};
+  void* ptrs[] = {h->zbuf, h->hbuf[0], h->hbuf[1], h->slots, h->partials, h->counters, h->status, h->xbuf,
+                  h->xseq, h->xdone,   h->xsdone,   h->vwords, h->vdone,    h->rbar,     h->gbar};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   free_packed(h);
@@ -1514,6 +1529,7 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   h.slots = reinterpret_cast<unsigned long long*>(take((size_t)c.batch * h.nslots * 8));
   h.partials = reinterpret_cast<float*>(take((size_t)2 * h.max_ctas * n_part * kTileM * 4));
   h.counters = reinterpret_cast<unsigned int*>(take((size_t)h.max_tiles * 4));
+  h.gbar = reinterpret_cast<unsigned int*>(take(64));
   if (off > kNoAllocScratchBytes)
     return fail(nullptr, DD_EINVAL,
                 "dd_rollout_noalloc: these shapes need %zu bytes of scratch; the static scratch holds %zu "
@@ -1531,7 +1547,8 @@ extern "C" int dd_rollout_noalloc(const dd_config* cfg, const dd_weights* w, int
   } zero[] = {{h.midbuf, (size_t)h.N2 * c.emb_dim * 2},
               {h.hbuf[0], (size_t)h.N1 * c.gru_hidden * es},
               {h.hbuf[1], (size_t)h.N1 * c.gru_hidden * es},
-              {h.counters, (size_t)h.max_tiles * 4}};
+              {h.counters, (size_t)h.max_tiles * 4},
+              {h.gbar, 64}};
   for (const auto& z : zero)
     if (cudaMemsetAsync(z.p, 0, z.n, st) != cudaSuccess)
       return fail(nullptr, DD_ECUDA, "dd_rollout_noalloc: cudaMemsetAsync failed");

@@ -36,7 +36,7 @@
 // unwinds all roles, drains in-flight TMA/MMA and frees TMEM.
 #pragma once
 
-#include "dd_ptx.cuh"
+#include "dd_cell_core.cuh"
 
 namespace dd {
 
@@ -61,37 +61,6 @@ constexpr uint32_t kSmemTail = 2048;            // barriers + flags + argmax red
 // outputs (z, base logits, the W_ih table): one 16-column chunk of a tile,
 // 16 x 128 elements of at most 4 bytes.
 constexpr uint32_t kXposeBytes = 16 * 128 * 4;
-
-constexpr int kMaxRanks = 8;
-
-// Argmax-word exchange between vocab-sharded ranks (one process per GPU).
-// Every rank owns an exchange buffer in its own HBM, mapped into every
-// other rank's address space (CUDA IPC, over NVLink):
-//   words[2][nslots][world][B]  u64 argmax words, by (call parity, slot, writer)
-//   flags[2][nslots][world]     u64 = the call's sequence number once written
-// The last CTA of a launch that finishes slots [xslot0, xslot1) writes this
-// rank's words into every rank's buffer, then the flags; the next cell kernel
-// waits (bounded) for all ranks' flags of its slot and takes the max word.
-struct Exchange {
-  int world, rank;                         // world == 1: no exchange
-  unsigned long long* peer[kMaxRanks];     // exchange buffer of rank j, as mapped here
-  const unsigned long long* seq;           // sequence number of the current call (device)
-  unsigned int* done;                      // per-slot count of finished CTAs (local)
-  int nslots, B;
-  unsigned long long timeout_ns;
-  // Sharded s / gh phase: rank j raises sflags[(par * nslots + slot) * world + j]
-  // (at u64 offset sflag_off of every buffer) once its slices of mid (byte
-  // offset mid_off) and gh (gh_off) for that step are written.
-  size_t sflag_off, mid_off, gh_off;
-  unsigned int* sdone;  // per-slot finished-CTA counters of the s / gh phase (local)
-};
-
-__device__ __forceinline__ size_t xchg_word(const Exchange& x, int par, int slot, int writer, int b) {
-  return (((size_t)par * x.nslots + slot) * x.world + writer) * x.B + b;
-}
-__device__ __forceinline__ size_t xchg_flag(const Exchange& x, int par, int slot, int writer) {
-  return (size_t)2 * x.nslots * x.world * x.B + ((size_t)par * x.nslots + slot) * x.world + writer;
-}
 
 struct GemvSeg {
   int rows;     // rows of W this phase streams
@@ -156,6 +125,12 @@ struct GemvParams {
   int v_off;
   long long base_ld, base_out_ld, base_voff;
   Exchange xchg;
+  // PH_FC2: run the step's GRU cell in this launch, after a grid-wide
+  // barrier (gbar: [0] arrival count, [1] generation) instead of in a launch
+  // of its own
+  int fused_cell;
+  unsigned int* gbar;
+  CellParams cell;
   int xslot0, xslot1;  // argmax words this launch publishes to every rank
   int sflag_slot;      // >= 0: this s / gh launch raises its step flag on every rank when done
   // fp32 heads (gemv_f32_kernel): the segments' weights and the X rows as
@@ -215,6 +190,33 @@ __device__ __forceinline__ bool wait_ns(uint64_t* bar, uint32_t parity, uint64_t
   while (!mbar_try_wait(bar, parity)) {
     if (globaltimer_ns() - t0 > limit_ns) return false;
   }
+  return true;
+}
+
+// One arrival of the calling CTA at a grid-wide barrier over n CTAs
+// (bar[0] arrival count, bar[1] generation), then, if `wait`, a bounded wait
+// for the last arrival.  The last CTA to arrive zeroes the count and bumps the
+// generation, so the barrier resets itself and a launch replayed from a CUDA
+// graph reuses it unchanged.  Every CTA of the grid must be resident at once
+// (a one-wave grid whose dependents launch only after all of its CTAs have
+// started).  Returns false if the wait gave up.
+__device__ __forceinline__ bool grid_barrier(unsigned int* bar, unsigned int n, bool wait) {
+  volatile unsigned int* gen = bar + 1;
+  const unsigned int g0 = *gen;  // read before arriving: it cannot have moved yet
+  __threadfence();
+  if (atomicAdd(bar, 1u) == n - 1) {
+    atomicExch(bar, 0u);
+    __threadfence();
+    atomicAdd(bar + 1, 1u);
+    return true;
+  }
+  if (!wait) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (*gen == g0) {
+    if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    __nanosleep(32);
+  }
+  __threadfence();
   return true;
 }
 
@@ -946,6 +948,25 @@ __global__ void __launch_bounds__(kThreads, 2)
     if constexpr (kPhase == PH_SGH) {
       if (p.xchg.world > 1 && p.sflag_slot >= 0 && named_bar_and(1, 128, *abort_flag == 0))
         publish_slices_done(p, ept, fin_flag);
+    }
+    if constexpr (kPhase == PH_FC2) {
+      if (p.fused_cell) {
+        // Every CTA's argmax words are final once all have arrived; then each
+        // CTA runs its share of the GRU step (a CTA that gave up arrives
+        // without waiting, so that the others are not held).
+        named_bar_sync(1, 128);
+        if (ept == 0) {
+          const bool aborted = *abort_flag != 0;
+          const bool ok = grid_barrier(p.gbar, gridDim.x, !aborted);
+          if (!ok) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
+          *fin_flag = ok && !aborted;
+        }
+        named_bar_sync(1, 128);
+        if (*fin_flag) {
+          const int n = p.cell.B * (p.cell.G / 8);
+          for (int idx = c * 128 + ept; idx < n; idx += G * 128) cell_apply<T>(p.cell, idx);
+        }
+      }
     }
   }
 

@@ -122,21 +122,26 @@ def apply_rope(x, cos, sin):
 
 
 class RaggedKVCache:
-    """Keys / values [B, kv_heads, capacity, head_dim] per layer and a valid
-    length per row.  ``write`` puts new entries at per-row positions."""
+    """Keys / values [B, kv_heads, capacity + 1, head_dim] per layer and a
+    valid length per row.  ``write`` puts new entries at per-row positions;
+    the extra last slot takes the entries that are not valid, so no call
+    needs the host to count them (the forward passes are free of host
+    synchronisation and can be captured in a CUDA graph)."""
 
     def __init__(self, layers: int, batch: int, kv_heads: int, capacity: int, head_dim: int, dtype, device):
-        self.k = [torch.zeros(batch, kv_heads, capacity, head_dim, dtype=dtype, device=device) for _ in range(layers)]
+        self.k = [torch.zeros(batch, kv_heads, capacity + 1, head_dim, dtype=dtype, device=device)
+                  for _ in range(layers)]
         self.v = [torch.zeros_like(t) for t in self.k]
         self.length = torch.zeros(batch, dtype=torch.long, device=device)
         self.capacity = capacity
 
     def write(self, layer: int, k, v, slots, valid):
         """k, v [B, kv_heads, T, D] to cache slots [B, T] where ``valid`` [B, T]."""
-        b_idx, t_idx = valid.nonzero(as_tuple=True)
-        s = slots[b_idx, t_idx]
-        self.k[layer][b_idx, :, s] = k[b_idx, :, t_idx]
-        self.v[layer][b_idx, :, s] = v[b_idx, :, t_idx]
+        B, _, T, _ = k.shape
+        b_idx = torch.arange(B, device=k.device).repeat_interleave(T)
+        s = torch.where(valid, slots, self.capacity).reshape(-1)
+        self.k[layer][b_idx, :, s] = k.transpose(1, 2).reshape(B * T, k.shape[1], k.shape[3])
+        self.v[layer][b_idx, :, s] = v.transpose(1, 2).reshape(B * T, v.shape[1], v.shape[3])
 
 
 def _attend(q, k, v, allowed, groups: int, scaling: float):
@@ -225,10 +230,10 @@ class TargetLM(nn.Module):
         """
         cfg = self.cfg
         B, T = ids.shape
-        start = cache.length
+        start = cache.length.clone()
         pos = start[:, None] + torch.arange(T, device=ids.device)[None]
         slots = pos.clamp(max=cache.capacity - 1)
-        L = int((start + valid.sum(1)).max())
+        L = cache.capacity  # keys past a row's length are masked
         key_pos = torch.arange(L, device=ids.device)
         allowed = key_pos[None, None, :] <= pos[:, :, None]
         allowed = allowed | ~valid[:, :, None]  # padded queries attend to everything (ignored)
@@ -252,7 +257,7 @@ class TargetLM(nn.Module):
         for li in feature_layers:
             if li == cfg.num_hidden_layers - 1:
                 feats[li] = x
-        cache.length = start + valid.sum(1)
+        cache.length.copy_(start + valid.sum(1))
         if logits_at is not None:
             x = x[torch.arange(B, device=ids.device), logits_at]
         logits = self.lm_head(x)
@@ -299,7 +304,7 @@ class DFlashBackbone(nn.Module):
         B, C, _ = ctx_features.shape
         T = noise.shape[1]
         dev = noise.device
-        start = cache.length
+        start = cache.length.clone()
         n_ctx = ctx_valid.sum(1)
         ctx_pos = start[:, None] + torch.arange(C, device=dev)[None]
         blk_pos = (start + n_ctx)[:, None] + torch.arange(T, device=dev)[None]
@@ -307,7 +312,7 @@ class DFlashBackbone(nn.Module):
         x = noise
         cos_c, sin_c = rope_tables(cfg, ctx_pos, x.dtype)
         cos_b, sin_b = rope_tables(cfg, blk_pos, x.dtype)
-        L = int((start + n_ctx).max()) + T
+        L = cache.capacity  # keys past a row's context + block are masked
         key_pos = torch.arange(L, device=dev)
         allowed = (key_pos[None, :] < (start + n_ctx + T)[:, None])[:, None, :].expand(B, T, L)
         slots_c = ctx_pos.clamp(max=cache.capacity - 1)
@@ -325,5 +330,5 @@ class DFlashBackbone(nn.Module):
             o = _attend(q, cache.k[li][:, :, :L], cache.v[li][:, :, :L], allowed, groups, a.cfg.head_dim ** -0.5)
             x = x + a.o_proj(o)
             x = x + layer.mlp(layer.post_attention_layernorm(x))
-        cache.length = start + n_ctx
+        cache.length.copy_(start + n_ctx)
         return self.norm(x)

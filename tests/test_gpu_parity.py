@@ -300,3 +300,26 @@ def test_nan_logits_win_like_torch_argmax(B):
     verify, base_out = r.draft_block(last, ph2)
     assert r.status() == 0
     assert bool(torch.isnan(base_out[b, 0]).all()) and int(verify[b, 1]) == 0
+
+
+@pytest.mark.parametrize("B,P", [(1, 1), (5, 2), (32, 1)])
+def test_fused_cell_matches_separate_cell_exactly(B, P, monkeypatch):
+    """The GRU cell run in the fc2 launch's tail (after its grid barrier) and
+    the cell in a launch of its own compute the same thing."""
+    H, G, E, V, S = 128, 128, 192, 2500, 15
+    draft, target = random_modules(H, G, E, V, seed=81 + B, fc2_std=0.08, gru_bias=True)
+    monkeypatch.setenv("DD_FUSE_CELL", "0")
+    rs = make_runner(draft, target, B, S, H, G, V, P)
+    monkeypatch.setenv("DD_FUSE_CELL", "1")
+    rf = make_runner(draft, target, B, S, H, G, V, P)
+    for seed in range(2):
+        prefix, ph, base = random_inputs(B, S, H, V, P, target, seed=seed)
+        assert torch.equal(rs(prefix, ph, base), rf(prefix, ph, base))
+    K = P - 1 + S
+    g = torch.Generator().manual_seed(6)
+    ph2 = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    last = torch.randint(0, V, (B,), generator=g).cuda()
+    vs, _ = rs.draft_block(last, ph2)
+    vf, _ = rf.draft_block(last, ph2)
+    assert torch.equal(vs, vf)
+    assert rs.status() == 0 and rf.status() == 0
