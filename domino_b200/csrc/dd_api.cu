@@ -124,7 +124,7 @@ struct dd_handle {
   int rollout_mode = 1;
   int min_units_per_cta = 8;
   int l2_prefetch_kb = 0;  // DD_L2_PREFETCH_KB: weight bytes per CTA prefetched into L2 past the ring
-  int fuse_cell = 1;       // DD_FUSE_CELL: the GRU cell runs in the fc2 launch's tail
+  int fuse_cell = 0;       // DD_FUSE_CELL=1: the GRU cell runs in the fc2 launch's tail (measured slower: off)
   unsigned int* gbar = nullptr;  // grid barrier of the fused cell: [0] count, [1] generation
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
