@@ -430,6 +430,8 @@ def run_ours(args):
             "device_status": status,
             "clocks": clk,
         }
+        if world == 1:
+            line["verify_roofline"] = measure_verify(device, V, peak)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, draft, target, ph_pool[0], last_pool[0], budget_s=30.0)
         print(json.dumps(line), flush=True)
@@ -437,6 +439,38 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def measure_verify(device, V, peak, B=16, K1=16, iters=20):
+    """Device time of the fused target verify + acceptance (dd_verify_accept)
+    over [B, K1, V] bf16 logits, rotating through four buffers (4 x 78 MB at
+    the default shape, more than L2), one CUDA-event pair around each launch."""
+    import torch
+
+    from domino_b200 import DraftCorrectionGraphRunner
+
+    draft, target = build_modules(64, 64, 64, V, device, seed=5)
+    r = DraftCorrectionGraphRunner(draft, target, B, 15, 64, 64, V, 1, device, use_graph=False)
+    g = torch.Generator(device=device).manual_seed(7)
+    logits = [torch.randn(B, K1, V, generator=g, device=device).to(torch.bfloat16) for _ in range(4)]
+    verify = torch.randint(0, V, (B, K1), generator=g, device=device)
+    for i in range(3):
+        r.verify_accept(logits[i % 4], verify)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(evs):
+        a.record()
+        r.verify_accept(logits[i % 4], verify)
+        b.record()
+    torch.cuda.synchronize()
+    us = statistics.mean(a.elapsed_time(b) for a, b in evs) * 1e3
+    nbytes = B * K1 * V * 2
+    r.close()
+    return {"kernel": "verify_accept_kernel (dd_verify_accept)", "logits": f"[{B}, {K1}, {V}] bf16",
+            "algorithmic_bytes_per_launch": nbytes, "avg_launch_us": round(us, 2),
+            "achieved": round(nbytes / (us / 1e6) / 1e9, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4),
+            "l2": "four logits buffers rotated (4 x the bytes above > 126 MB L2)"}
 
 
 # ---------------------------------------------------------------- CPU leg

@@ -386,9 +386,22 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     const bool xp = a.xpose != nullptr && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & (4 * sizeof(T) - 1)) == 0;
     T* S = reinterpret_cast<T*>(a.xpose);
     const int w4 = ept >> 5;
+    // Whole tiles with one accumulator (the common case) read TMEM one chunk
+    // ahead: chunk ch + 1's load is in flight while chunk ch is converted,
+    // staged and stored.
+    const bool ahead = !a.combine && a.nacc == 1;
+    float nxt[16];
+    if (ahead) tmem_ld16(a.taddr, nxt);
     for (int ch = 0; ch < nchunks; ++ch) {
       float v[16];
-      acc_chunk(a, ch, v);
+      if (ahead) {
+        tmem_ld_wait_regs(nxt);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = nxt[j];
+        if (ch + 1 < nchunks) tmem_ld16(a.taddr + (ch + 1) * 16, nxt);
+      } else {
+        acc_chunk(a, ch, v);
+      }
       T vals[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) vals[j] = IO::from_f(v[j] + bias);

@@ -187,6 +187,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// tcgen05.wait::ld that also names the 16 registers of a load in flight, so
+// that no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_ld_wait_regs(float (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
+                 "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]), "+f"(v[15])
+               :
+               : "memory");
+}
+
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzle: rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart
 // (SBO = 1024), LBO unused (1), descriptor version 1, layout SWIZZLE_128B.
