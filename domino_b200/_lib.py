@@ -24,6 +24,9 @@ DD_F32 = 2
 DD_STATUS_TIMEOUT = 1
 DD_STATUS_BAD_TOKEN = 2
 DD_STATUS_NO_ARGMAX = 4
+# dd_set_middle kinds (include/domino_draft.h)
+DD_MIDDLE_SILU, DD_MIDDLE_IDENTITY, DD_MIDDLE_RELU, DD_MIDDLE_GELU = 0, 1, 2, 3
+DD_MIDDLE_GELU_TANH, DD_MIDDLE_TANH, DD_MIDDLE_SIGMOID, DD_MIDDLE_SILU_ROUNDED = 4, 5, 6, 7
 
 EXPORTS = (
     "dd_create", "dd_set_weights", "dd_build_table", "dd_rollout", "dd_draft_block",
@@ -31,7 +34,7 @@ EXPORTS = (
     "dd_set_timing", "dd_read_timing", "dd_rollout_noalloc", "dd_noalloc_status",
     "dd_get_exchange_buffer", "dd_ipc_export", "dd_ipc_open", "dd_ipc_close", "dd_set_vocab_shard",
     "dd_set_exchange_timeout", "dd_verify_accept", "dd_set_weight_layout", "dd_set_rollout_mode",
-    "dd_set_trace",
+    "dd_set_trace", "dd_set_middle",
 )
 PHASES = {1: "z", 2: "zlm", 3: "gh", 4: "sgh", 5: "fc2", 6: "table", 7: "cell", 8: "gather", 9: "rollout"}
 
@@ -114,6 +117,7 @@ def load() -> ctypes.CDLL:
         lib.dd_set_weight_layout.argtypes = [vp, ctypes.c_int]
         lib.dd_set_rollout_mode.argtypes = [vp, ctypes.c_int]
         lib.dd_set_trace.argtypes = [vp, ctypes.POINTER(DDTrace)]
+        lib.dd_set_middle.argtypes = [vp, ctypes.c_int]
         lib.dd_read_timing.argtypes = [vp, vp, vp, i32]
         for name in EXPORTS:
             if name not in ("dd_last_error", "dd_version"):

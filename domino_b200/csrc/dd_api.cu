@@ -36,6 +36,11 @@
 
 using namespace dd;
 
+static_assert(DD_MIDDLE_SILU == MID_SILU && DD_MIDDLE_IDENTITY == MID_IDENTITY && DD_MIDDLE_RELU == MID_RELU &&
+                  DD_MIDDLE_GELU == MID_GELU && DD_MIDDLE_GELU_TANH == MID_GELU_TANH && DD_MIDDLE_TANH == MID_TANH &&
+                  DD_MIDDLE_SIGMOID == MID_SIGMOID && DD_MIDDLE_SILU_ROUNDED == MID_SILU_ROUNDED,
+              "the header's middle kinds and the kernels' must agree");
+
 namespace {
 
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -124,6 +129,7 @@ struct dd_handle {
   int rollout_mode = 1;
   int min_units_per_cta = 8;
   int l2_prefetch_kb = 0;  // DD_L2_PREFETCH_KB: weight bytes per CTA prefetched into L2 past the ring
+  int middle = MID_SILU;    // dd_set_middle: the correction MLP's activation (and numerics)
   int fuse_cell = 0;       // DD_FUSE_CELL=1: the GRU cell runs in the fc2 launch's tail (measured slower: off)
   unsigned int* gbar = nullptr;  // grid barrier of the fused cell: [0] count, [1] generation
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
@@ -407,6 +413,7 @@ GemvParams base_params(const dd_handle* h) {
   p.base_voff = h->v_off;
   p.xchg = make_exchange(h);
   p.sflag_slot = -1;
+  p.middle = h->middle;
   return p;
 }
 
@@ -663,6 +670,7 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
       cp.out_ld = out_ld;
       cp.out_col = out_col0 + t;
       cp.write_h = last ? 0 : 1;
+      cp.torch_cell = h->middle != MID_SILU;  // the PyTorch branch's cell (the prefix GRU is nn.GRU in both)
       cp.gh = h->ghbuf;
       cp.h_in = h->hbuf[cur];
       cp.h_out = h->hbuf[cur ^ 1];
@@ -697,7 +705,8 @@ int run_rollout_persistent(dd_handle* h, const int64_t* ids, int ids_ld, int n_p
   const dd_config& c = h->cfg;
   const int n_prefix_total = n_prefix_ids + npre;
   const int nphases = 1 + 2 * (n_prefix_total - 1) + 3 * c.steps;
-  if (h->rollout_mode != 0 || h->world > 1 || h->tracing || nphases > kMaxRollPhases) return DD_EUNSUPPORTED;
+  if (h->rollout_mode != 0 || h->world > 1 || h->tracing || h->middle != MID_SILU || nphases > kMaxRollPhases)
+    return DD_EUNSUPPORTED;
   static RollParams rp;  // ~10 KB: kept off the stack; the handle is not thread-safe anyway
   memset(&rp, 0, sizeof(rp));
   GemvParams& gp = rp.gp;
@@ -1084,6 +1093,13 @@ int dd_set_weights(dd_handle* h, const dd_weights* w) {
 int dd_set_rollout_mode(dd_handle* h, int mode) {
   if (!h || mode < 0 || mode > 1) return DD_EINVAL;
   h->rollout_mode = mode;
+  return DD_OK;
+}
+
+int dd_set_middle(dd_handle* h, int middle) {
+  if (!h) return DD_EINVAL;
+  if (middle < MID_SILU || middle > MID_SILU_ROUNDED) return fail(h, DD_EINVAL, "unknown middle kind %d", middle);
+  h->middle = middle;
   return DD_OK;
 }
 

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(256) gather_slices_kernel(const GatherParams p
 // finish (done counter) decodes all rows, runs the prefix match, and clears
 // the words and the counter for the next call.
 constexpr int kVerifyThreads = 256;
-constexpr int kVerifyChunk = 8192;
+constexpr int kVerifyChunk = 32768;  // vocab entries per CTA: 16 16-byte loads per thread in flight
 
 template <typename L>
 __device__ __forceinline__ float logit_f(L v);
@@ -128,11 +128,21 @@ __device__ __forceinline__ float logit_f<__nv_bfloat16>(__nv_bfloat16 v) { retur
 template <>
 __device__ __forceinline__ float logit_f<__half>(__half v) { return __half2float(v); }
 
-template <typename L>
-__device__ __forceinline__ unsigned long long max_key(unsigned long long best, L v, int idx) {
-  const unsigned long long k = argmax_key(logit_f<L>(v), (uint32_t)idx);
-  return k > best ? k : best;
-}
+// Running (value, index) argmax over increasing indices: a strictly larger
+// value replaces the best, so the first of equal maxima stays, and a NaN
+// replaces a number but not an earlier NaN (torch.argmax's order).
+struct ArgmaxRun {
+  float v = -INFINITY;
+  int i = -1;
+  __device__ __forceinline__ void see(float x, int idx) {
+    const bool take = (x > v) || (x != x && v == v) || i < 0;
+    v = take ? x : v;
+    i = take ? idx : i;
+  }
+  __device__ __forceinline__ unsigned long long key() const {
+    return i < 0 ? 0ull : argmax_key(v, (uint32_t)i);
+  }
+};
 
 template <typename L>
 __global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* logits, int V, int B, int K1,
@@ -150,11 +160,13 @@ __global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* 
   const L* src = logits + (size_t)row * V;
   // 16-byte loads over the aligned middle of [v0, v1); rows of odd length
   // start anywhere, so the first `head` elements and the tail go one by one.
+  // Each thread sees its indices in increasing order: head, vectors, tail.
   constexpr int kVec = 16 / (int)sizeof(L);
   const int head = min(v1 - v0, (int)(((16u - (reinterpret_cast<uintptr_t>(src + v0) & 15u)) & 15u) / sizeof(L)));
   const int nvec = (v1 - v0 - head) / kVec;
   const int vtail = v0 + head + nvec * kVec;
-  unsigned long long best = 0ull;
+  ArgmaxRun run;
+  if ((int)threadIdx.x < head) run.see(logit_f<L>(src[v0 + threadIdx.x]), v0 + threadIdx.x);
   const uint4* vsrc = reinterpret_cast<const uint4*>(src + v0 + head);
 #pragma unroll 4
   for (int i = threadIdx.x; i < nvec; i += kVerifyThreads) {
@@ -162,10 +174,10 @@ __global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* 
     const L* e = reinterpret_cast<const L*>(&raw);
     const int vb = v0 + head + i * kVec;
 #pragma unroll
-    for (int j = 0; j < kVec; ++j) best = max_key<L>(best, e[j], vb + j);
+    for (int j = 0; j < kVec; ++j) run.see(logit_f<L>(e[j]), vb + j);
   }
-  if ((int)threadIdx.x < head) best = max_key<L>(best, src[v0 + threadIdx.x], v0 + threadIdx.x);
-  for (int v = vtail + threadIdx.x; v < v1; v += kVerifyThreads) best = max_key<L>(best, src[v], v);
+  for (int v = vtail + threadIdx.x; v < v1; v += kVerifyThreads) run.see(logit_f<L>(src[v]), v);
+  unsigned long long best = run.key();
   best = warp_max_u64(best);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = best;
   __syncthreads();

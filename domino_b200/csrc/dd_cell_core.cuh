@@ -52,6 +52,7 @@ struct CellParams {
   int out_ld, out_col;
   int h_zero;                   // h = 0 and gh = b_hh (first prefix token)
   int write_h;
+  int torch_cell;               // 1: the reference's PyTorch-branch cell, every op rounded, tanh (domino.py:423-430)
   const void* table;            // [V, 3G], row stride table_ld
   long long table_ld;
   const void* gh;               // [B, 3G]
@@ -155,12 +156,25 @@ __device__ __forceinline__ void cell_apply(const CellParams& p, int idx) {
     load8<T>(reinterpret_cast<const T*>(p.h_in) + (size_t)b * G + g0, h);
   }
   alignas(16) T outv[8];
+  if (p.torch_cell) {
+    // r = sigmoid(i_r + h_r); z = sigmoid(i_z + h_z); n = tanh(i_n + r * h_n);
+    // h' = (1 - z) * n + z * h, each op's result in the state dtype
+    auto rd = [](float x) { return io<T>::to_f(io<T>::from_f(x)); };
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const float r = sigmoidf_(ir[i] + hr[i]);
-    const float z = sigmoidf_(iz[i] + hz[i]);
-    const float n = 2.0f * sigmoidf_(2.0f * (in_[i] + r * hn[i])) - 1.0f;
-    outv[i] = io<T>::from_f((1.0f - z) * n + z * h[i]);
+    for (int i = 0; i < 8; ++i) {
+      const float r = rd(sigmoidf_(rd(ir[i] + hr[i])));
+      const float z = rd(sigmoidf_(rd(iz[i] + hz[i])));
+      const float n = rd(tanhf(rd(in_[i] + rd(r * hn[i]))));
+      outv[i] = io<T>::from_f(rd(rd(1.0f - z) * n) + rd(z * h[i]));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float r = sigmoidf_(ir[i] + hr[i]);
+      const float z = sigmoidf_(iz[i] + hz[i]);
+      const float n = 2.0f * sigmoidf_(2.0f * (in_[i] + r * hn[i])) - 1.0f;
+      outv[i] = io<T>::from_f((1.0f - z) * n + z * h[i]);
+    }
   }
   constexpr int kVecs = (int)sizeof(T) * 8 / 16;
 #pragma unroll

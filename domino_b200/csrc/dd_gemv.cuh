@@ -104,6 +104,7 @@ struct GemvParams {
   int z_rows_per_b, z_pos_off;
   void* mid_out;
   void* s_out;  // optional trace: s[b * E + e] (rounded), as the epilogue uses it
+  int middle;   // MID_*: the activation between fc1 and fc2, and with it the numerics (dd_ptx.cuh)
   // EPI_GH
   void* gh_out;
   const void* b_hh;
@@ -386,22 +387,9 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     const bool xp = a.xpose != nullptr && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & (4 * sizeof(T) - 1)) == 0;
     T* S = reinterpret_cast<T*>(a.xpose);
     const int w4 = ept >> 5;
-    // Whole tiles with one accumulator (the common case) read TMEM one chunk
-    // ahead: chunk ch + 1's load is in flight while chunk ch is converted,
-    // staged and stored.
-    const bool ahead = !a.combine && a.nacc == 1;
-    float nxt[16];
-    if (ahead) tmem_ld16(a.taddr, nxt);
     for (int ch = 0; ch < nchunks; ++ch) {
       float v[16];
-      if (ahead) {
-        tmem_ld_wait_regs(nxt);
-#pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = nxt[j];
-        if (ch + 1 < nchunks) tmem_ld16(a.taddr + (ch + 1) * 16, nxt);
-      } else {
-        acc_chunk(a, ch, v);
-      }
+      acc_chunk(a, ch, v);
       T vals[16];
 #pragma unroll
       for (int j = 0; j < 16; ++j) vals[j] = IO::from_f(v[j] + bias);
@@ -476,10 +464,17 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           if (p.s_out) ((T*)p.s_out)[(size_t)b * p.E + row] = s_rounded;
           const float s = IO::to_f(s_rounded);
           const float z = zv[j];
-          const float pre = z + s;
-          const float mid = pre * sigmoidf_(pre);
-          const T hi = IO::from_f(mid);
-          const T lo = IO::from_f(mid - IO::to_f(hi));
+          T hi, lo;
+          if (p.middle == MID_SILU) {
+            const float pre = z + s;
+            const float mid = pre * sigmoidf_(pre);
+            hi = IO::from_f(mid);
+            lo = IO::from_f(mid - IO::to_f(hi));
+          } else {
+            // the PyTorch branch: mid = middle(z + s) in the weight dtype, one row
+            hi = IO::from_f(middle_act(p.middle, IO::to_f(IO::from_f(z + s))));
+            lo = IO::from_f(0.0f);
+          }
           ((T*)p.mid_out)[(size_t)(2 * b) * p.E + row] = hi;
           ((T*)p.mid_out)[(size_t)(2 * b + 1) * p.E + row] = lo;
         }
@@ -513,7 +508,9 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           const int b = ch * 8 + i;
           unsigned long long key = 0ull;
           if (b < p.B && valid && ch < nchunks) {
-            const float logit = v[2 * i] + v[2 * i + 1] + bias + basev[i];
+            float logit = v[2 * i] + v[2 * i + 1] + bias + basev[i];
+            if (p.middle != MID_SILU)  // bias = F.linear(mid, fc2, b2); logits = base + bias, each in the dtype
+              logit = IO::to_f(IO::from_f(IO::to_f(IO::from_f(v[2 * i] + v[2 * i + 1] + bias)) + basev[i]));
             key = argmax_key(logit, (uint32_t)(p.v_off + row));
           }
           k[b] = key;
@@ -542,7 +539,11 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
             const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
             float logit = v[2 * b] + v[2 * b + 1];
             logit += bias;
-            logit += IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+            const float basev = IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+            if (p.middle != MID_SILU)  // bias = F.linear(mid, fc2, b2); logits = base + bias, each in the dtype
+              logit = IO::to_f(IO::from_f(IO::to_f(IO::from_f(logit)) + basev));
+            else
+              logit += basev;
             key = argmax_key(logit, (uint32_t)(p.v_off + row));
           }
           key = warp_max_u64(key);

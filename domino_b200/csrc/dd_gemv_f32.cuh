@@ -42,11 +42,11 @@ __device__ __forceinline__ void epilogue_f32(const GemvParams& p, int kind, int 
     const float bias = p.b_hh ? static_cast<const float*>(p.b_hh)[row] : 0.0f;
     static_cast<float*>(p.gh_out)[gn * p.G3 + row] = v + bias;
   } else if (phase_has<kPhase>(EPI_SPROJ_MID) && kind == EPI_SPROJ_MID) {
-    // s = h W_s^T (fp32, domino.py:397); mid = SiLU(z_t + s) (domino.py:95-96)
+    // s = h W_s^T (fp32, domino.py:397); mid = middle(z_t + s) (domino.py:95-96, 406-408)
     if (p.s_out) static_cast<float*>(p.s_out)[gn * p.E + row] = v;
     const size_t zrow = (size_t)gn * p.z_rows_per_b + p.z_pos_off + p.t;
     const float pre = static_cast<const float*>(p.z_src)[zrow * p.E + row] + v;
-    static_cast<float*>(p.mid_out)[gn * p.E + row] = pre * sigmoidf_(pre);
+    static_cast<float*>(p.mid_out)[gn * p.E + row] = middle_act(p.middle, pre);
   }
 }
 

@@ -187,15 +187,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// tcgen05.wait::ld that also names the 16 registers of a load in flight, so
-// that no use of them can be scheduled before the wait.
-__device__ __forceinline__ void tmem_ld_wait_regs(float (&v)[16]) {
-  asm volatile("tcgen05.wait::ld.sync.aligned;"
-               : "+f"(v[0]), "+f"(v[1]), "+f"(v[2]), "+f"(v[3]), "+f"(v[4]), "+f"(v[5]), "+f"(v[6]), "+f"(v[7]),
-                 "+f"(v[8]), "+f"(v[9]), "+f"(v[10]), "+f"(v[11]), "+f"(v[12]), "+f"(v[13]), "+f"(v[14]), "+f"(v[15])
-               :
-               : "memory");
-}
 
 // Shared-memory matrix descriptor for a K-major tile written by TMA with
 // 128-byte swizzle: rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart
@@ -264,5 +255,32 @@ struct io<float> {
 
 // Logistic in fp32 from expf, the form 1 / (1 + exp(-x)).
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// The middle of the correction MLP (embed_proj = Linear, middle, Linear).
+// MID_SILU is the reference's fused path: SiLU(z + s) in fp32 fed to an fp32
+// fc2 contraction (code/kernel/domino.py:58-136).  Every other kind is its
+// PyTorch branch (domino.py:406-431): each op rounded to the weight dtype.
+enum MiddleKind : int {
+  MID_SILU = 0,
+  MID_IDENTITY = 1,
+  MID_RELU = 2,
+  MID_GELU = 3,       // 0.5 x (1 + erf(x / sqrt 2))
+  MID_GELU_TANH = 4,  // 0.5 x (1 + tanh(sqrt(2 / pi) (x + 0.044715 x^3)))
+  MID_TANH = 5,
+  MID_SIGMOID = 6,
+  MID_SILU_ROUNDED = 7,  // a SiLU that the reference does not fuse (e.g. followed by Dropout)
+};
+
+__device__ __forceinline__ float middle_act(int kind, float x) {
+  switch (kind) {
+    case MID_IDENTITY: return x;
+    case MID_RELU: return x < 0.0f ? 0.0f : x;  // NaN stays NaN
+    case MID_GELU: return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
+    case MID_GELU_TANH: return 0.5f * x * (1.0f + tanhf(0.79788456080286536f * (x + 0.044715f * x * x * x)));
+    case MID_TANH: return tanhf(x);
+    case MID_SIGMOID: return sigmoidf_(x);
+    default: return x * sigmoidf_(x);
+  }
+}
 
 }  // namespace dd

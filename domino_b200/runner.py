@@ -55,6 +55,39 @@ def _middle_is_silu(middle: nn.Module) -> bool:
     )
 
 
+def middle_kind(middle: nn.Module) -> int:
+    """The kernels' code for ``embed_proj``'s middle.
+
+    One ``nn.SiLU`` (alone or as the single child of a Sequential) is the
+    reference's fused path (code/kernel/domino.py:280-289); every other middle
+    runs its PyTorch branch (domino.py:406-431), which the kernels reproduce for
+    an identity, ReLU, GELU (erf or tanh), Tanh, Sigmoid or SiLU, with Dropout
+    and Identity modules around it (eval mode).  Anything else raises
+    ``NotImplementedError``: there is no fallback that would compute it another way.
+    """
+    if _middle_is_silu(middle):
+        return _lib.DD_MIDDLE_SILU
+    mods = list(middle.children()) if isinstance(middle, nn.Sequential) else [middle]
+    acts = [m for m in mods if not isinstance(m, (nn.Identity, nn.Dropout))]
+    if not acts:
+        return _lib.DD_MIDDLE_IDENTITY
+    if len(acts) == 1:
+        a = acts[0]
+        if isinstance(a, nn.ReLU):
+            return _lib.DD_MIDDLE_RELU
+        if isinstance(a, nn.GELU):
+            return _lib.DD_MIDDLE_GELU_TANH if a.approximate == "tanh" else _lib.DD_MIDDLE_GELU
+        if isinstance(a, nn.Tanh):
+            return _lib.DD_MIDDLE_TANH
+        if isinstance(a, nn.Sigmoid):
+            return _lib.DD_MIDDLE_SIGMOID
+        if isinstance(a, nn.SiLU):
+            return _lib.DD_MIDDLE_SILU_ROUNDED
+    raise NotImplementedError(
+        f"embed_proj middle {middle!r}: the B200 runner implements an identity, ReLU, GELU, Tanh, Sigmoid or SiLU "
+        "middle (with Dropout / Identity around it)")
+
+
 def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
@@ -109,11 +142,7 @@ class DraftCorrectionGraphRunner:
                 f"Correction MLP input dim mismatch: got {fc1.in_features}, "
                 f"expected {expected_in} = hidden_dim + gru_hidden_dim."
             )
-        if not _middle_is_silu(self.middle):
-            raise NotImplementedError(
-                "the B200 runner fuses SiLU(z + s) into the fc2 contraction; "
-                f"embed_proj middle {self.middle!r} is not a single nn.SiLU"
-            )
+        self._middle_kind = middle_kind(self.middle)
         gru = draft_model.prefix_gru
         if gru.num_layers != 1 or gru.bidirectional:
             raise ValueError("prefix_gru must be a single-layer unidirectional nn.GRU")
@@ -170,6 +199,7 @@ class DraftCorrectionGraphRunner:
         with torch.cuda.device(device):
             _lib.check(self._lib.dd_create(ctypes.byref(cfg), device.index, ctypes.byref(handle)), None, "dd_create")
         self._h = handle
+        _lib.check(self._lib.dd_set_middle(self._h, self._middle_kind), self._h, "dd_set_middle")
 
         with torch.cuda.device(device):
             stream = torch.cuda.current_stream(device)

@@ -102,6 +102,24 @@ int dd_set_weights(dd_handle* h, const dd_weights* w);
  * give identical tokens. */
 int dd_set_rollout_mode(dd_handle* h, int mode);
 
+/* The middle of the correction MLP, embed_proj = (Linear, middle, Linear)
+ * (code/kernel/domino.py:15-50).  DD_MIDDLE_SILU (default) is the reference's
+ * fused path: SiLU(z + s) in fp32 into an fp32 fc2 contraction (domino.py:58-136).
+ * For any other middle the reference runs its PyTorch branch
+ * (domino.py:406-431), and so does this library: mid = middle(z + s), the fc2
+ * logits and base + logits, and every op of the GRU cell (with tanh) rounded
+ * to the weight dtype.  DD_MIDDLE_SILU_ROUNDED is a SiLU the reference does not
+ * fuse (a middle of several modules, e.g. SiLU then Dropout). */
+#define DD_MIDDLE_SILU 0
+#define DD_MIDDLE_IDENTITY 1
+#define DD_MIDDLE_RELU 2
+#define DD_MIDDLE_GELU 3       /* erf form */
+#define DD_MIDDLE_GELU_TANH 4  /* tanh approximation */
+#define DD_MIDDLE_TANH 5
+#define DD_MIDDLE_SIGMOID 6
+#define DD_MIDDLE_SILU_ROUNDED 7
+int dd_set_middle(dd_handle* h, int middle);
+
 /* packed = 0 (default: stream the caller's row-major weights in place, no
  * extra memory) or 1 (stream the packed copy with 1-D bulk copies; measured
  * equal speed at the default launch shape; DD_PACK_WEIGHTS=1 in the

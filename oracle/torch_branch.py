@@ -1,19 +1,24 @@
-"""The reference's PyTorch branch of the draft step, restated in torch CPU ops.
+"""The reference's PyTorch branch of the draft step, restated in torch ops.
 
-TEST INFRASTRUCTURE ONLY: the CPU leg of the benchmark (``bench.py
---impl reference`` and the ``cpu_baseline`` record); never part of the
-product.  The numpy oracle (oracle/draft_oracle.py) is the parity checker; this
-module exists for speed.  It runs the reference's CPU op sequence (torch's
-bf16 kernels on the host, AMX where the CPU has it), so that the timed CPU
-baseline is as fast as the reference's own code on the same host, which the
-numpy restatement in fp32 is not.
+TEST INFRASTRUCTURE ONLY, never part of the product, in two roles:
+
+* the CPU leg of the benchmark (``bench.py --impl reference`` and the
+  ``cpu_baseline`` record): it runs the reference's CPU op sequence (torch's
+  bf16 kernels on the host, AMX where the CPU has it), so that the timed CPU
+  baseline is as fast as the reference's own code on the same host, which the
+  numpy restatement in fp32 (oracle/draft_oracle.py) is not;
+* the parity checker of heads whose ``embed_proj`` middle is not a single SiLU:
+  for those the reference always takes this branch, so on a GPU these ops (CUDA
+  torch kernels) are the reference's own arithmetic.  For SiLU heads the numpy
+  oracle, which restates the Triton branch, is the checker.
 
 What it restates, op for op:
 
-* ``_forward_impl`` with ``HAS_TRITON = False`` (code/kernel/domino.py:374-431):
-  ``z = F.linear(hiddens, W_z, b1)`` (381-385); ``h = GRU(embed(prefix_ids))``
-  (387-391); per step ``s = F.linear(h, W_s)`` (397), ``mid = SiLU(z_t + s)``
-  (406-408), ``logits = base_t + F.linear(mid, fc2, b2)`` (409-410),
+* ``_forward_impl``'s PyTorch branch (code/kernel/domino.py:374-431), which
+  the reference takes without Triton and, on any device, for a middle that is
+  not a single SiLU: ``z = F.linear(hiddens, W_z, b1)`` (381-385);
+  ``h = GRU(embed(prefix_ids))`` (387-391); per step ``s = F.linear(h, W_s)``
+  (397), ``mid = middle(z_t + s)`` (406-408), ``logits = base_t + F.linear(mid, fc2, b2)`` (409-410),
   ``argmax`` (411), then ``gi = table[token]``, ``gh = F.linear(h, W_hh, b_hh)``
   and the GRU cell with ``tanh`` (418-431);
 * the table ``F.linear(embed, W_ih, b_ih)`` (domino.py:322-327), built once;
@@ -27,7 +32,7 @@ tests/golden/rollout_*.npz (``tokens_torch``), bit for bit
 from __future__ import annotations
 
 from dataclasses import dataclass
-from typing import Optional
+from typing import Callable, Optional
 
 import torch
 import torch.nn.functional as F
@@ -46,6 +51,7 @@ class TorchHead:
     lm_head: Optional[torch.Tensor] = None  # [V, H]
     fc1_bias: Optional[torch.Tensor] = None
     fc2_bias: Optional[torch.Tensor] = None
+    middle: Callable = F.silu         # embed_proj's middle module (domino.py:406-408)
 
     @property
     def w_hh(self):
@@ -57,20 +63,25 @@ class TorchHead:
 
 
 @torch.inference_mode()
-def head_from_modules(draft, target, table: Optional[torch.Tensor] = None) -> TorchHead:
-    """A CPU ``TorchHead`` from the reference's modules (code/kernel/domino.py:260-327).
+def head_from_modules(draft, target, table: Optional[torch.Tensor] = None, device="cpu") -> TorchHead:
+    """A ``TorchHead`` from the reference's modules (code/kernel/domino.py:260-327),
+    on the CPU by default.  On a GPU the same ops run the reference's PyTorch
+    branch with CUDA torch kernels, which is the reference's own arithmetic for
+    a head whose middle is not a single SiLU.
 
     ``table`` may be given (for example built on a GPU and copied here) to skip
     the one-time ``embed @ W_ih^T`` on the host.
     """
-    cpu = torch.device("cpu")
+    cpu = torch.device(device)
     fc1, fc2 = draft.embed_proj[0], draft.embed_proj[-1]
     H = target.model.embed_tokens.weight.shape[1]
     gru_src = draft.prefix_gru
     gru = torch.nn.GRU(gru_src.input_size, gru_src.hidden_size, num_layers=1, batch_first=True,
                        bias=gru_src.bias, dtype=gru_src.weight_ih_l0.dtype)
     gru.load_state_dict({k: v.detach().to(cpu) for k, v in gru_src.state_dict().items()})
-    gru.eval()
+    gru = gru.to(cpu).eval()
+    mods = list(draft.embed_proj.children())
+    middle = torch.nn.Sequential(*mods[1:-1]).to(cpu).eval() if len(mods) > 2 else torch.nn.Identity()
     w1 = fc1.weight.detach().to(cpu)
     embed = target.model.embed_tokens.weight.detach().to(cpu)
     if table is None:
@@ -82,25 +93,39 @@ def head_from_modules(draft, target, table: Optional[torch.Tensor] = None) -> To
         lm_head=lm.weight.detach().to(cpu) if lm is not None else None,
         fc1_bias=fc1.bias.detach().to(cpu) if fc1.bias is not None else None,
         fc2_bias=fc2.bias.detach().to(cpu) if fc2.bias is not None else None,
+        middle=middle,
     )
 
 
 @torch.inference_mode()
 def rollout(w: TorchHead, prefix_ids: torch.Tensor, parallel_hiddens: torch.Tensor,
-            base_logits: torch.Tensor) -> torch.Tensor:
+            base_logits: torch.Tensor, teacher_tokens: Optional[torch.Tensor] = None, record=None) -> torch.Tensor:
     """[B, 1+p] ids, [B, S, H] hiddens, [B, S, V] base logits -> [B, S] tokens
-    (code/kernel/domino.py:374-431, PyTorch branch)."""
+    (code/kernel/domino.py:374-431, PyTorch branch).
+
+    With ``teacher_tokens`` [B, S] the GRU is fed those tokens instead of the
+    argmax (teacher forcing); with ``record`` (a dict) it also records, per
+    step, the logit of the fed token and the top logit (``chosen``, ``top``,
+    [B, S] fp32) for the near-tie rule of the parity tests."""
     B, S, _ = parallel_hiddens.shape
+    dev = parallel_hiddens.device
     z_all = F.linear(parallel_hiddens, w.w_z, w.fc1_bias)                # 381-385
     _, hidden = w.gru(F.embedding(prefix_ids, w.embed))                  # 387-391
-    out = torch.zeros(B, S, dtype=torch.long)
+    out = torch.zeros(B, S, dtype=torch.long, device=dev)
+    chosen = torch.zeros(B, S, device=dev)
+    top = torch.zeros(B, S, device=dev)
     for t in range(S):
         h = hidden.squeeze(0)
         s = F.linear(h, w.w_s, None)                                     # 397
-        mid = F.silu(z_all[:, t:t + 1, :] + s.unsqueeze(1))              # 406-408
+        mid = w.middle(z_all[:, t:t + 1, :] + s.unsqueeze(1))            # 406-408
         logits = base_logits[:, t:t + 1, :] + F.linear(mid, w.fc2, w.fc2_bias)  # 409-410
         tok = torch.argmax(logits, dim=-1)                               # 411
         out[:, t:t + 1] = tok
+        if teacher_tokens is not None:
+            tok = teacher_tokens[:, t:t + 1].to(dev)
+        if record is not None:
+            top[:, t] = logits.float().amax(-1)[:, 0]
+            chosen[:, t] = logits.float()[:, 0].gather(1, tok)[:, 0]
         if t + 1 < S:                                                    # 416-431
             gi = w.table[tok.squeeze(-1)]
             gh = F.linear(h, w.w_hh, w.b_hh)
@@ -109,6 +134,8 @@ def rollout(w: TorchHead, prefix_ids: torch.Tensor, parallel_hiddens: torch.Tens
             zg = torch.sigmoid(gi[:, g:2 * g] + gh[:, g:2 * g])
             n = torch.tanh(gi[:, 2 * g:] + r * gh[:, 2 * g:])
             hidden = ((1.0 - zg) * n + zg * h).unsqueeze(0)
+    if record is not None:
+        record["chosen"], record["top"] = chosen, top
     return out
 
 

@@ -198,6 +198,42 @@ def rollout_case(name, *, seed, B, H, G, E, V, S, P, dtype, fc1_bias=False, fc2_
     print(f"{name}: triton vs torch-branch token agreement {agree:.3f}")
 
 
+def middle_case(name, *, seed, B, H, G, E, V, S, P, middle: str):
+    """A head whose embed_proj middle is not a single SiLU: the reference's
+    runner then takes its PyTorch branch (code/kernel/domino.py:406-431) on
+    any device.  Records the weights, the inputs and its tokens."""
+    torch.manual_seed(seed)
+    draft = TinyDraftHead(H, G, E, V, False, False, False)
+    if middle == "identity":
+        draft.embed_proj = nn.Sequential(draft.embed_proj[0], draft.embed_proj[2])
+    else:
+        draft.embed_proj[1] = {"gelu": nn.GELU(), "relu": nn.ReLU(), "tanh": nn.Tanh()}[middle]
+    target = TinyTarget(H, V)
+    with torch.no_grad():
+        for p in list(draft.parameters()) + list(target.parameters()):
+            p.normal_(0.0, 0.02 if p.dim() == 2 else 0.05)
+        target.model.embed_tokens.weight.normal_(0.0, 1.0)
+        draft.embed_proj[-1].weight.normal_(0.0, 0.1)  # a correction large enough to move the argmax
+    draft, target = draft.to(torch.bfloat16), target.to(torch.bfloat16)
+    prefix_ids = torch.randint(0, V, (B, P))
+    ph = torch.randn(B, S, H).to(torch.bfloat16)
+    with torch.no_grad():
+        base = target.lm_head(ph)
+    r = _make_runner(draft, target, B, S, H, G, V, P, triton=True)
+    assert not r._can_triton_fuse, "a non-SiLU middle must take the PyTorch branch"
+    out = r(prefix_ids, ph, base)
+    np.savez_compressed(
+        OUT / f"{name}.npz",
+        meta=np.array([B, H, G, E, V, S, P, 0, 0, 0], np.int64), dtype=np.array("bf16"), middle=np.array(middle),
+        fc1=_np(draft.embed_proj[0].weight), fc2=_np(draft.embed_proj[-1].weight),
+        w_ih=_np(draft.prefix_gru.weight_ih_l0), w_hh=_np(draft.prefix_gru.weight_hh_l0),
+        embed=_np(target.model.embed_tokens.weight), lm_head=_np(target.lm_head.weight),
+        prefix_ids=prefix_ids.numpy(), parallel_hiddens=_np(ph), base_logits=_np(base),
+        tokens_torch=out.numpy(),
+    )
+    print(f"{name}: PyTorch-branch tokens {out.tolist()}")
+
+
 def accept_case():
     """Synthetic (verify_ids, posterior) pairs through dflash.py:473-484."""
     g = torch.Generator().manual_seed(7)
@@ -425,6 +461,8 @@ def main():
                      dtype="bf16", fc1_bias=True, fc2_bias=True, gru_bias=True)
         rollout_case("rollout_fp32_b1", seed=3, B=1, H=64, G=64, E=96, V=600, S=15, P=1, dtype="fp32")
         accept_case()
+        middle_case("middle_gelu_b2", seed=11, B=2, H=64, G=64, E=96, V=600, S=15, P=1, middle="gelu")
+        middle_case("middle_identity_b2", seed=12, B=2, H=64, G=48, E=80, V=600, S=13, P=2, middle="identity")
     spec_generate_trace("spec_trace_random", seed=4, mode="random", max_new_tokens=10)
     spec_generate_trace("spec_trace_full_accept", seed=5, mode="full", max_new_tokens=40)
     spec_generate_trace("spec_trace_partial", seed=38, mode="partial", max_new_tokens=20)

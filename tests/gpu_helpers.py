@@ -76,13 +76,21 @@ def random_modules(H, G, E, V, *, seed=0, dtype=torch.bfloat16, device="cuda", f
     return draft.to(device=device, dtype=dtype).eval(), target.to(device=device, dtype=dtype).eval()
 
 
+MIDDLES = {"gelu": nn.GELU, "relu": nn.ReLU, "tanh": nn.Tanh}
+
+
 def modules_from_fixture(fx, device="cuda"):
     B, H, G, E, V, S, P, fb1, fb2, gb = (int(x) for x in fx["meta"])
     draft = DraftHead(H, G, E, V, bool(fb1), bool(fb2), bool(gb))
+    middle = str(fx["middle"]) if "middle" in fx else "silu"
+    if middle == "identity":
+        draft.embed_proj = nn.Sequential(draft.embed_proj[0], draft.embed_proj[2])
+    elif middle != "silu":
+        draft.embed_proj[1] = MIDDLES[middle]()
     target = Target(H, V)
     with torch.no_grad():
         draft.embed_proj[0].weight.copy_(torch.from_numpy(as_f32(fx["fc1"])))
-        draft.embed_proj[2].weight.copy_(torch.from_numpy(as_f32(fx["fc2"])))
+        draft.embed_proj[-1].weight.copy_(torch.from_numpy(as_f32(fx["fc2"])))
         draft.prefix_gru.weight_ih_l0.copy_(torch.from_numpy(as_f32(fx["w_ih"])))
         draft.prefix_gru.weight_hh_l0.copy_(torch.from_numpy(as_f32(fx["w_hh"])))
         target.model.embed_tokens.weight.copy_(torch.from_numpy(as_f32(fx["embed"])))
@@ -90,7 +98,7 @@ def modules_from_fixture(fx, device="cuda"):
         if fb1:
             draft.embed_proj[0].bias.copy_(torch.from_numpy(as_f32(fx["fc1_bias"])))
         if fb2:
-            draft.embed_proj[2].bias.copy_(torch.from_numpy(as_f32(fx["fc2_bias"])))
+            draft.embed_proj[-1].bias.copy_(torch.from_numpy(as_f32(fx["fc2_bias"])))
         if gb:
             draft.prefix_gru.bias_ih_l0.copy_(torch.from_numpy(as_f32(fx["b_ih"])))
             draft.prefix_gru.bias_hh_l0.copy_(torch.from_numpy(as_f32(fx["b_hh"])))

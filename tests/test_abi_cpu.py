@@ -82,7 +82,7 @@ def test_runner_validates_like_the_reference():
     with pytest.raises(ValueError):
         _mk(nn.Sequential(nn.Linear(15, 12), nn.SiLU(), nn.Linear(12, 10)))
     with pytest.raises(NotImplementedError):
-        _mk(nn.Sequential(nn.Linear(16, 12), nn.GELU(), nn.Linear(12, 10)))
+        _mk(nn.Sequential(nn.Linear(16, 12), nn.Softplus(), nn.Linear(12, 10)))
     with pytest.raises(NotImplementedError):
         _mk(nn.Sequential(nn.Linear(16, 12), nn.SiLU(), nn.Linear(12, 10)), dtype=torch.float64)
     with pytest.raises(ValueError):
@@ -90,3 +90,24 @@ def test_runner_validates_like_the_reference():
             gru=nn.GRU(8, 8, num_layers=2, batch_first=True))
     with pytest.raises(RuntimeError):
         _mk(nn.Sequential(nn.Linear(16, 12), nn.SiLU(), nn.Linear(12, 10)), device="cpu")
+
+
+def test_middle_kinds_follow_the_reference_branches():
+    """One SiLU (alone or the single child of a Sequential) is the reference's
+    fused path (code/kernel/domino.py:280-289); everything else is its PyTorch
+    branch, which the kernels implement for these activations."""
+    from domino_b200 import _lib
+    from domino_b200.runner import middle_kind
+
+    assert middle_kind(nn.SiLU()) == _lib.DD_MIDDLE_SILU
+    assert middle_kind(nn.Sequential(nn.SiLU())) == _lib.DD_MIDDLE_SILU
+    assert middle_kind(nn.Sequential(nn.SiLU(), nn.Dropout(0.1))) == _lib.DD_MIDDLE_SILU_ROUNDED
+    assert middle_kind(nn.Identity()) == _lib.DD_MIDDLE_IDENTITY
+    assert middle_kind(nn.Sequential(nn.GELU())) == _lib.DD_MIDDLE_GELU
+    assert middle_kind(nn.GELU(approximate="tanh")) == _lib.DD_MIDDLE_GELU_TANH
+    assert middle_kind(nn.ReLU()) == _lib.DD_MIDDLE_RELU
+    assert middle_kind(nn.Tanh()) == _lib.DD_MIDDLE_TANH
+    assert middle_kind(nn.Sequential(nn.Dropout(0.0), nn.Sigmoid())) == _lib.DD_MIDDLE_SIGMOID
+    for bad in (nn.Softplus(), nn.Sequential(nn.ReLU(), nn.Tanh()), nn.LeakyReLU()):
+        with pytest.raises(NotImplementedError):
+            middle_kind(bad)

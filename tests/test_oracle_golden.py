@@ -164,3 +164,21 @@ def test_torch_branch_matches_reference_pytorch_branch(case):
     out = TB.rollout(w, torch.from_numpy(fx["prefix_ids"]), torch.from_numpy(as_f32(fx["parallel_hiddens"])).to(dt),
                      torch.from_numpy(as_f32(fx["base_logits"])).to(dt))
     assert np.array_equal(out.numpy(), fx["tokens_torch"])
+
+
+@pytest.mark.parametrize("case", ["middle_gelu_b2", "middle_identity_b2"])
+def test_torch_branch_matches_reference_for_other_middles(case):
+    """Heads whose middle is not a single SiLU: the reference's runner takes its
+    PyTorch branch, and the torch restatement (the checker of the kernels for
+    these heads) gives its tokens."""
+    import torch
+
+    from oracle import torch_branch as TB
+    from tests.gpu_helpers import modules_from_fixture
+
+    fx = load(case)
+    draft, target = modules_from_fixture(fx, device="cpu")
+    w = TB.head_from_modules(draft, target)
+    out = TB.rollout(w, torch.from_numpy(fx["prefix_ids"]), torch.from_numpy(as_f32(fx["parallel_hiddens"])).bfloat16(),
+                     torch.from_numpy(as_f32(fx["base_logits"])).bfloat16())
+    assert np.array_equal(out.numpy(), fx["tokens_torch"])
