@@ -40,6 +40,7 @@ static_assert(DD_MIDDLE_SILU == MID_SILU && DD_MIDDLE_IDENTITY == MID_IDENTITY &
                   DD_MIDDLE_GELU == MID_GELU && DD_MIDDLE_GELU_TANH == MID_GELU_TANH && DD_MIDDLE_TANH == MID_TANH &&
                   DD_MIDDLE_SIGMOID == MID_SIGMOID && DD_MIDDLE_SILU_ROUNDED == MID_SILU_ROUNDED,
               "the header's middle kinds and the kernels' must agree");
+static_assert(kMaxVerifyK1 == 64, "dd_verify_accept's position limit and its kernel's shared arrays must agree");
 
 namespace {
 
@@ -130,7 +131,8 @@ struct dd_handle {
   int min_units_per_cta = 8;
   int l2_prefetch_kb = 0;  // DD_L2_PREFETCH_KB: weight bytes per CTA prefetched into L2 past the ring
   int middle = MID_SILU;    // dd_set_middle: the correction MLP's activation (and numerics)
-  int fuse_cell = 0;       // DD_FUSE_CELL=1: the GRU cell runs in the fc2 launch's tail (measured slower: off)
+  int fuse_cell = 0;
+  int base_stage = 1;      // DD_BASE_STAGE: fc2 loads base-logit tiles by TMA at batch > 4       // DD_FUSE_CELL=1: the GRU cell runs in the fc2 launch's tail (measured slower: off)
   unsigned int* gbar = nullptr;  // grid barrier of the fused cell: [0] count, [1] generation
   // dd_verify_accept scratch: per-(row, position) argmax words + done counter
   static constexpr int kMaxVerifyPositions = 64;
@@ -197,6 +199,23 @@ int encode_kmajor(dd_handle* h, CUtensorMap* m, const void* ptr, int dtype, long
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(h, DD_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return DD_OK;
+}
+
+// 3-D map over base logits [B, rows_per_b, ld] (2-byte elements) with boxes of
+// 128 columns x 1 position x B rows: one tile's base logits for one step.
+int encode_base_map(dd_handle* h, CUtensorMap* m, const void* ptr, int dtype, long long ld, long long rows_per_b,
+                    int batch) {
+  int rc = ensure_encoder(h);
+  if (rc) return rc;
+  cuuint64_t dims[3] = {(cuuint64_t)ld, (cuuint64_t)rows_per_b, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(ld * rows_per_b * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)kTileM, 1u, (cuuint32_t)batch};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, dtype == DD_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                        const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(h, DD_ECUDA, "cuTensorMapEncodeTiled (base logits) failed (%d)", (int)r);
   return DD_OK;
 }
 
@@ -268,10 +287,12 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   p.stage_bytes = kATileBytes + p.b_bytes;
   const uint32_t ring_budget =
       p.N > 64 ? 196u * 1024u : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
-  p.stages = std::max(4, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  // At least four stages, three when the base-logit buffers take the room
+  // of the fourth (batch 32), so that two CTAs still share an SM.
+  p.stages = std::max(p.base_stage_bytes ? 3 : 4, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
   p.l2_prefetch_units = (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
   p.xpose_bytes = (kPhase == PH_ZLM || kPhase == PH_Z || kPhase == PH_TABLE) ? kXposeBytes : 0u;
-  const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes;
+  const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes + 2 * p.base_stage_bytes;
   if ((size_t)p.stages * p.stage_bytes + fixed > 227 * 1024) p.stages = (227 * 1024 - fixed) / p.stage_bytes;
   p.acc_slots = 2;  // the epilogue of one tile overlaps the next tile's MMAs (2 x 256 columns at most)
   // Up to four accumulators per slot within the per-CTA TMEM budget, so that
@@ -535,6 +556,18 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
   const dd_config& c = h->cfg;
   int rc;
   int cur = 0;
+  // fc2 at more than four batch rows: each tile's base logits arrive by TMA
+  // (16-byte row strides and column offset needed; 2-byte types only).
+  CUtensorMap tm_base;
+  uint32_t base_stage = 0;
+  if constexpr (!std::is_same<T, float>::value) {
+    if (c.batch > 4 && h->base_stage && (base_ld % 8) == 0 && (base_voff % 8) == 0 &&
+        (reinterpret_cast<uintptr_t>(base) & 15) == 0) {
+      rc = encode_base_map(h, &tm_base, base, c.dtype, base_ld, positions, c.batch);
+      if (rc) return rc;
+      base_stage = (uint32_t)c.batch * kTileM * 2;
+    }
+  }
   // h0 from the first prefix token, zero state.
   {
     CellParams cp;
@@ -683,7 +716,9 @@ int run_rollout(dd_handle* h, const int64_t* ids, int ids_ld, int n_prefix_ids, 
         p.gbar = h->gbar;
         p.cell = cp;
       }
-      rc = launch_gemv<T, PH_FC2>(h, h->tm_fc2, nullptr, h->tm_mid, p, PhaseClass::Big, true, st);
+      p.base_stage_bytes = base_stage;
+      rc = launch_gemv<T, PH_FC2>(h, h->tm_fc2, base_stage ? &tm_base : nullptr, h->tm_mid, p, PhaseClass::Big, true,
+                                  st);
       if (!rc && !fuse) rc = launch_cell<T>(h, cp, st);
       if (!rc && !last) rc = trace_copy(h, h->trace.h, n_prefix_total + t, h->hbuf[cur ^ 1], c.batch, c.gru_hidden, st);
       if (rc) return rc;
@@ -906,7 +941,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
-// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL) over the defaults of a fresh
+// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -929,6 +964,7 @@ void read_launch_env(dd_handle* h) {
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", d.tmem_cols_per_cta, 32, 512);
   h->l2_prefetch_kb = env_int("DD_L2_PREFETCH_KB", d.l2_prefetch_kb, 0, 4096);
   h->fuse_cell = env_int("DD_FUSE_CELL", d.fuse_cell, 0, 1);
+  h->base_stage = env_int("DD_BASE_STAGE", d.base_stage, 0, 1);
 }
 
 }  // namespace

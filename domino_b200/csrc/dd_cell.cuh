@@ -117,7 +117,8 @@ __global__ void __launch_bounds__(256) gather_slices_kernel(const GatherParams p
 // finish (done counter) decodes all rows, runs the prefix match, and clears
 // the words and the counter for the next call.
 constexpr int kVerifyThreads = 256;
-constexpr int kVerifyChunk = 32768;  // vocab entries per CTA: 16 16-byte loads per thread in flight
+constexpr int kVerifyChunk = 32768;
+constexpr int kMaxVerifyK1 = 64;  // positions per row (the handle's word buffer holds B x 64)  // vocab entries per CTA: 16 16-byte loads per thread in flight
 
 template <typename L>
 __device__ __forceinline__ float logit_f(L v);
@@ -192,25 +193,27 @@ __global__ void __launch_bounds__(kVerifyThreads) verify_accept_kernel(const L* 
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int b = threadIdx.x; b < B; b += kVerifyThreads) {
-    int a = 0;
-    bool matching = true;
-    for (int j = 0; j < K1; ++j) {
-      const unsigned long long k = __ldcg(words + (size_t)b * K1 + j);
-      if (!k) atomicOr(status, 4u /* DD_STATUS_NO_ARGMAX */);
-      const int64_t tok = k ? (int64_t)argmax_key_index(k) : 0;
-      posterior[(size_t)b * K1 + j] = tok;
-      if (matching && j + 1 < K1 && verify[(size_t)b * K1 + j + 1] == tok) {
-        ++a;
-      } else {
-        matching = false;
-      }
-    }
-    accept[b] = a;
-    bonus[b] = posterior[(size_t)b * K1 + a];
+  // The last CTA: one word per thread decoded into the posterior (and shared
+  // memory), then the prefix match of every row from shared memory.
+  __shared__ int32_t post[kMaxBatch * kMaxVerifyK1];
+  __shared__ int64_t ver[kMaxBatch * kMaxVerifyK1];
+  const int n = B * K1;
+  for (int i = threadIdx.x; i < n; i += kVerifyThreads) {
+    const unsigned long long k = __ldcg(words + i);
+    if (!k) atomicOr(status, 4u /* DD_STATUS_NO_ARGMAX */);
+    const int32_t tok = k ? (int32_t)argmax_key_index(k) : 0;
+    post[i] = tok;
+    ver[i] = verify[i];
+    posterior[i] = tok;
+    words[i] = 0ull;  // ready for the next call
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < B * K1; i += kVerifyThreads) words[i] = 0ull;
+  for (int b = threadIdx.x; b < B; b += kVerifyThreads) {
+    int a = 0;
+    while (a + 1 < K1 && ver[b * K1 + a + 1] == (int64_t)post[b * K1 + a]) ++a;
+    accept[b] = a;
+    bonus[b] = post[b * K1 + a];
+  }
   if (threadIdx.x == 0) *done = 0u;
 }
 

@@ -82,6 +82,10 @@ struct GemvParams {
   int n_valid;       // X rows of this pass that carry data (<= N)
   long long units;   // (tile, k-chunk) units in this pass
   int stages;
+  // PH_FC2 with more than four batch rows: the producer also loads each tile's
+  // base logits [B, 128] by TMA (the tensor map in tmA1) into one of two
+  // buffers of base_stage_bytes after the tail; 0 = plain loads in the epilogue
+  uint32_t base_stage_bytes;
   int l2_prefetch_units;  // weight tiles past the ring this CTA prefetches into L2 before waiting on its predecessor
   uint32_t stage_bytes;
   uint32_t b_bytes;
@@ -237,6 +241,7 @@ struct AccView {
   void* xpose;         // shared staging chunk for row-contiguous stores, or null
   long long row0;      // global row of the tile's first row
   long long row_end;   // end of the segment's rows (exclusive, global)
+  const void* bsm;     // PH_FC2 staging: this tile's base logits [B][128] in shared memory, or null
 };
 
 // Four consecutive elements (8 or 16 bytes, aligned) from shared to global memory.
@@ -499,8 +504,12 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
           const int b = ch * 8 + i;
           basev[i] = 0.0f;
           if (b < p.B && valid) {
-            const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
-            basev[i] = IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+            if (a.bsm) {
+              basev[i] = IO::to_f(static_cast<const T*>(a.bsm)[b * kTileM + a.r]);
+            } else {
+              const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
+              basev[i] = IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
+            }
           }
         }
 #pragma unroll
@@ -679,14 +688,19 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* accf = empty + kMaxStages;
   uint64_t* acce = accf + 2;
   uint64_t* drain = acce + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* bfull = drain + 1;   // [2] base-logit tile landed (PH_FC2 staging)
+  uint64_t* bempty = bfull + 2;  // [2] base-logit buffer read by the epilogue
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   volatile int* fin_flag = abort_flag + 1;
   // tail layout: [0, 512) barriers and flags, [512, 1024) counters, [1024, 2048) argmax reduction
-  static_assert((2 * kMaxStages + 5) * 8 + 16 <= 512, "barrier block overflows its slot");
+  static_assert((2 * kMaxStages + 9) * 8 + 16 <= 512, "barrier block overflows its slot");
   static_assert(1024 + 4 * kMaxBatch * 8 <= kSmemTail, "reduction block overflows the tail");
   long long* issued = reinterpret_cast<long long*>(tail + 512);
   long long* consumed = issued + 1;
+  long long* bissued = issued + 2;    // base tiles loaded by the producer
+  long long* bconsumed = issued + 3;  // base tiles waited for by the epilogue
+  uint8_t* bstage = tail + kSmemTail + p.xpose_bytes;  // [2][base_stage_bytes]
   unsigned long long* red = reinterpret_cast<unsigned long long*>(tail + 1024);  // [4][kMaxBatch]
 
   const int warp = threadIdx.x >> 5;
@@ -708,15 +722,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&acce[s], 128);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bfull[s], 1);
+      mbar_init(&bempty[s], 1);
+    }
     *abort_flag = 0;
     *fin_flag = 0;
     *issued = 0;
     *consumed = 0;
+    *bissued = 0;
+    *bconsumed = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA0);
-    if (p.nseg > 1) prefetch_tmap(&tmA1);
+    if (p.nseg > 1 || p.base_stage_bytes) prefetch_tmap(&tmA1);
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
@@ -799,10 +819,31 @@ __global__ void __launch_bounds__(kThreads, 2)
         load_b(i, kb);
         if (++kb == KC) kb = 0;
       }
+      // Base-logit tiles (PH_FC2 staging), in tile order, two buffers: the
+      // base of every tile up to `upto` is loaded once its buffer is free.
+      // They come after the wait: the base logits may be written by an
+      // earlier launch of the same call.
+      long long btile = tile_begin;
+      const long long tile_last = n_my > 0 ? (u_end - 1) / KC : tile_begin - 1;  // no units: no base tiles
+      auto base_upto = [&](long long upto) -> bool {
+        if (!p.base_stage_bytes) return true;
+        for (; btile <= upto && btile <= tile_last; ++btile) {
+          const long long n = btile - tile_begin;
+          const int bs = (int)(n & 1);
+          if (!mbar_wait_bounded(&bempty[bs], (uint32_t)(((n >> 1) & 1) ^ 1), abort_flag)) return false;
+          mbar_arrive_expect_tx(&bfull[bs], p.base_stage_bytes);
+          tma_load_3d(bstage + (size_t)bs * p.base_stage_bytes, &tmA1, &bfull[bs],
+                      (int)(p.base_voff + btile * kTileM), p.base_pos_off + p.t, 0);
+          *bissued = n + 1;
+        }
+        return true;
+      };
+      bool ok = base_upto((u_begin + (pre > 0 ? pre - 1 : 0)) / KC);
       int stage = pre == p.stages ? 0 : pre;
       uint32_t parity = pre == p.stages ? 1u : 0u;
       long long it = pre;
-      for (; it < n_my; ++it) {
+      for (; ok && it < n_my; ++it) {
+        if (!base_upto(tile)) break;
         if (!mbar_wait_bounded(&empty[stage], parity ^ 1u, abort_flag)) break;
         mbar_arrive_expect_tx(&full[stage], kATileBytes + p.b_bytes);
         load_a(stage, tile, kc);
@@ -912,6 +953,19 @@ __global__ void __launch_bounds__(kThreads, 2)
       a.U = U;
       a.G = G;
       a.KC = KC;
+      a.bsm = nullptr;
+      int bslot = 0;
+      if constexpr (kPhase == PH_FC2) {
+        if (p.base_stage_bytes) {
+          // every tile's base load is waited for (in order), finished here or not
+          const long long n = tile - u_begin / KC;
+          bslot = (int)(n & 1);
+          const bool landed = mbar_wait_bounded(&bfull[bslot], (uint32_t)((n >> 1) & 1), abort_flag);
+          if (!named_bar_and(1, 128, landed)) break;
+          if (ept == 0) *bconsumed = n + 1;
+          a.bsm = bstage + (size_t)bslot * p.base_stage_bytes;
+        }
+      }
 
       bool finish = true;
       if (kc0 > 0 || kc1 < KC) {
@@ -947,6 +1001,12 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       }
       if (finish) epilogue_tile<T, kPhase>(p, a, sg.kind, row, valid, q, lane, red, ept);
+      if constexpr (kPhase == PH_FC2) {
+        if (p.base_stage_bytes) {
+          named_bar_sync(1, 128);  // all reads of this base buffer done
+          if (ept == 0) mbar_arrive(&bempty[bslot]);
+        }
+      }
 
       tc_fence_before();
       mbar_arrive(&acce[slot]);
@@ -995,6 +1055,8 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (warp == 0 && lane == 0) {
       for (long long it = *consumed; it < *issued; ++it)
         wait_ns(&full[it % p.stages], (uint32_t)((it / p.stages) & 1), 100ull * 1000 * 1000);
+      for (long long n = *bconsumed; n < *bissued; ++n)
+        wait_ns(&bfull[n & 1], (uint32_t)((n >> 1) & 1), 100ull * 1000 * 1000);
     }
     if (threadIdx.x == 0) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
     __syncthreads();

@@ -67,8 +67,11 @@ def middle_kind(middle: nn.Module) -> int:
     """
     if _middle_is_silu(middle):
         return _lib.DD_MIDDLE_SILU
-    mods = list(middle.children()) if isinstance(middle, nn.Sequential) else [middle]
-    acts = [m for m in mods if not isinstance(m, (nn.Identity, nn.Dropout))]
+
+    def flat(m):
+        return [x for c in m.children() for x in flat(c)] if isinstance(m, nn.Sequential) else [m]
+
+    acts = [m for m in flat(middle) if not isinstance(m, (nn.Identity, nn.Dropout))]
     if not acts:
         return _lib.DD_MIDDLE_IDENTITY
     if len(acts) == 1:

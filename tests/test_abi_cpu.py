@@ -102,6 +102,7 @@ def test_middle_kinds_follow_the_reference_branches():
     assert middle_kind(nn.SiLU()) == _lib.DD_MIDDLE_SILU
     assert middle_kind(nn.Sequential(nn.SiLU())) == _lib.DD_MIDDLE_SILU
     assert middle_kind(nn.Sequential(nn.SiLU(), nn.Dropout(0.1))) == _lib.DD_MIDDLE_SILU_ROUNDED
+    assert middle_kind(nn.Sequential(nn.Sequential(nn.SiLU(), nn.Dropout(0.1)))) == _lib.DD_MIDDLE_SILU_ROUNDED
     assert middle_kind(nn.Identity()) == _lib.DD_MIDDLE_IDENTITY
     assert middle_kind(nn.Sequential(nn.GELU())) == _lib.DD_MIDDLE_GELU
     assert middle_kind(nn.GELU(approximate="tanh")) == _lib.DD_MIDDLE_GELU_TANH
