@@ -227,21 +227,21 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* bar, unsigned int n, 
 
 // Context an epilogue thread needs to read its (possibly split) accumulator.
 struct AccView {
-  uint32_t taddr;      // TMEM address of this thread's lane, column 0 of the slot
-  int nacc;            // accumulators of the slot, N columns apart
-  bool combine;        // split tile finished here: sum partials of all segments
-  int nseg, myseg, c_lo;
-  long long T;
-  const float* partials;
-  int N;
-  int r;               // row within the tile
-  long long U;
-  int G, KC;
-  uint32_t bar;        // named barrier of the 128 epilogue threads
-  void* xpose;         // shared staging chunk for row-contiguous stores, or null
-  long long row0;      // global row of the tile's first row
-  long long row_end;   // end of the segment's rows (exclusive, global)
-  const void* bsm;     // PH_FC2 staging: this tile's base logits [B][128] in shared memory, or null
+  uint32_t taddr = 0;        // TMEM address of this thread's lane, column 0 of the slot
+  int nacc = 1;              // accumulators of the slot, N columns apart
+  bool combine = false;      // split tile finished here: sum partials of all segments
+  int nseg = 1, myseg = 0, c_lo = 0;
+  long long T = 0;
+  const float* partials = nullptr;
+  int N = 0;
+  int r = 0;                 // row within the tile
+  long long U = 0;
+  int G = 0, KC = 0;
+  uint32_t bar = 1;          // named barrier of the 128 epilogue threads
+  void* xpose = nullptr;     // shared staging chunk for row-contiguous stores, or null
+  long long row0 = 0;        // global row of the tile's first row
+  long long row_end = 0;     // end of the segment's rows (exclusive, global)
+  const void* bsm = nullptr; // PH_FC2 staging: this tile's base logits [B][128] in shared memory, or null
 };
 
 // Four consecutive elements (8 or 16 bytes, aligned) from shared to global memory.
@@ -493,6 +493,17 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
       // One key per batch row in every lane, then a transposing butterfly:
       // each round halves the keys a lane holds, so 31 shuffles leave lane l
       // with the warp's maximum for batch row l (instead of 5 per row).
+      // Base logit of batch row b: bptr[b * bstride], from the tile's staged
+      // block in shared memory or from global memory.
+      const T* bptr;
+      long long bstride;
+      if (a.bsm) {
+        bptr = static_cast<const T*>(a.bsm) + a.r;
+        bstride = kTileM;
+      } else {
+        bptr = (const T*)p.base_src + ((size_t)p.base_pos_off + p.t) * p.base_ld + p.base_voff + row;
+        bstride = (long long)p.base_rows_per_b * p.base_ld;
+      }
       unsigned long long k[kMaxBatch];
 #pragma unroll
       for (int ch = 0; ch < kMaxBatch / 8; ++ch) {  // a 16-column chunk holds 8 rows (hi, lo)
@@ -503,14 +514,7 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
         for (int i = 0; i < 8; ++i) {
           const int b = ch * 8 + i;
           basev[i] = 0.0f;
-          if (b < p.B && valid) {
-            if (a.bsm) {
-              basev[i] = IO::to_f(static_cast<const T*>(a.bsm)[b * kTileM + a.r]);
-            } else {
-              const size_t brow = (size_t)b * p.base_rows_per_b + p.base_pos_off + p.t;
-              basev[i] = IO::load((const T*)p.base_src + brow * p.base_ld + p.base_voff + row);
-            }
-          }
+          if (b < p.B && valid) basev[i] = IO::load(bptr + b * bstride);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
