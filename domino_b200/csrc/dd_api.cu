@@ -138,6 +138,7 @@ struct dd_handle {
   static constexpr int kMaxVerifyPositions = 64;
   unsigned long long* vwords = nullptr;
   unsigned int* vdone = nullptr;
+  int verify_per_sm[3] = {0, 0, 0};  // resident verify CTAs per SM, by logits dtype (f32, f16, bf16)
   // Opt-in state trace (dd_set_trace): per-step copies of z, h, gh and s.
   bool tracing = false;
   dd_trace trace{};
@@ -971,6 +972,37 @@ void read_launch_env(dd_handle* h) {
 
 // ============================================================================ C ABI
 
+// One verify launch.  The vocab of a row is cut into `parts` chunks so that
+// the grid (parts x rows) is at most one wave of resident CTAs, with at least
+// one group of vectors per thread in a chunk; chunks start on whole vectors.
+template <typename T>
+static int launch_verify(dd_handle* h, const T* logits, int dt, int32_t k1, const int64_t* verify_ids,
+                         int64_t* posterior_out, int32_t* accept_out, int64_t* bonus_out, void* stream) {
+  const dd_config& c = h->cfg;
+  if (!h->verify_per_sm[dt]) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, verify_accept_kernel<T>, kVerifyThreads, 0) !=
+            cudaSuccess ||
+        per_sm < 1)
+      return fail(h, DD_ECUDA, "verify_accept: occupancy query failed");
+    h->verify_per_sm[dt] = per_sm;
+  }
+  constexpr int kVec = 16 / (int)sizeof(T);
+  const long long rows = (long long)c.batch * k1;
+  const long long slots = (long long)h->num_sms * h->verify_per_sm[dt];
+  const int min_chunk = kVerifyThreads * kVerifyGroup * kVec;
+  int parts = (int)std::max<long long>(1, slots / rows);
+  parts = std::min(parts, std::max(1, c.vocab / min_chunk));
+  const int chunk = ceil_div(ceil_div(c.vocab, parts), kVec) * kVec;
+  Launch launch(dim3(ceil_div(c.vocab, chunk), (unsigned)rows), dim3(kVerifyThreads), 0,
+           reinterpret_cast<cudaStream_t>(stream));
+  const cudaError_t e = cudaLaunchKernelEx(&launch.cfg, verify_accept_kernel<T>, logits, c.vocab, chunk, c.batch, (int)k1,
+                                           verify_ids, posterior_out, accept_out, bonus_out, h->vwords, h->vdone,
+                                           h->status);
+  if (e != cudaSuccess) return fail(h, DD_ECUDA, "verify_accept launch: %s", cudaGetErrorString(e));
+  return DD_OK;
+}
+
 extern "C" {
 
 const char* dd_version(void) { return "domino_b200 0.1 (sm_100a, tcgen05 weight streaming)"; }
@@ -1294,26 +1326,14 @@ int dd_verify_accept(dd_handle* h, const void* target_logits, int32_t logits_dty
     return fail(h, DD_EINVAL, "dd_verify_accept: %d positions outside [1, %d]", k1, dd_handle::kMaxVerifyPositions);
   int rc = use_device(h);
   if (rc) return rc;
-  const dd_config& c = h->cfg;
-  dim3 grid(ceil_div(c.vocab, kVerifyChunk), c.batch * k1);
-  Launch L(grid, dim3(kVerifyThreads), 0, reinterpret_cast<cudaStream_t>(stream));
-  cudaError_t e;
-  if (logits_dtype == DD_F32)
-    e = cudaLaunchKernelEx(&L.cfg, verify_accept_kernel<float>, static_cast<const float*>(target_logits), c.vocab,
-                           c.batch, (int)k1, verify_ids, posterior_out, accept_out, bonus_out, h->vwords, h->vdone,
-                           h->status);
-  else if (logits_dtype == DD_FP16)
-    e = cudaLaunchKernelEx(&L.cfg, verify_accept_kernel<__half>, static_cast<const __half*>(target_logits), c.vocab,
-                           c.batch, (int)k1, verify_ids, posterior_out, accept_out, bonus_out, h->vwords, h->vdone,
-                           h->status);
-  else if (logits_dtype == DD_BF16)
-    e = cudaLaunchKernelEx(&L.cfg, verify_accept_kernel<__nv_bfloat16>,
-                           static_cast<const __nv_bfloat16*>(target_logits), c.vocab, c.batch, (int)k1, verify_ids,
-                           posterior_out, accept_out, bonus_out, h->vwords, h->vdone, h->status);
-  else
-    return fail(h, DD_EINVAL, "dd_verify_accept: logits dtype %d", logits_dtype);
-  if (e != cudaSuccess) return fail(h, DD_ECUDA, "verify_accept launch: %s", cudaGetErrorString(e));
-  return DD_OK;
+  if (logits_dtype == DD_F32) return launch_verify<float>(h, static_cast<const float*>(target_logits), 0, k1,
+                                                          verify_ids, posterior_out, accept_out, bonus_out, stream);
+  if (logits_dtype == DD_FP16) return launch_verify<__half>(h, static_cast<const __half*>(target_logits), 1, k1,
+                                                            verify_ids, posterior_out, accept_out, bonus_out, stream);
+  if (logits_dtype == DD_BF16)
+    return launch_verify<__nv_bfloat16>(h, static_cast<const __nv_bfloat16*>(target_logits), 2, k1, verify_ids,
+                                        posterior_out, accept_out, bonus_out, stream);
+  return fail(h, DD_EINVAL, "dd_verify_accept: logits dtype %d", logits_dtype);
 }
 
 int dd_get_exchange_buffer(dd_handle* h, void** dev_ptr, uint64_t* bytes) {

@@ -86,3 +86,50 @@ def test_verify_accept_nan_ranks_first_like_torch_argmax(dtype):
     assert post[0, 2] == 7 and post[1, 5] == V - 1 and post[2, 0] == 3 and post[2, 7] == 0
     assert np.array_equal(post.cpu().numpy(), np.argmax(logits.float().cpu().numpy(), axis=-1))
     r.close()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_verify_accept_signed_zeros_and_infinities(dtype):
+    """-0 and +0 are equal for torch.argmax, so the first zero wins whatever
+    its sign; rows of -inf (all, or all but one) and tied +inf maxima keep
+    the first index (code/dflash.py:472)."""
+    B, K1, V = 2, 16, 20011
+    r = _runner(B, V)
+    _, verify, _ = _case(B, K1, V, dtype, 11)
+    logits = torch.full((B, K1, V), -1.0, device="cuda", dtype=dtype)
+    logits[0, 0, 100] = -0.0
+    logits[0, 0, 50] = 0.0                  # +0 first: 50
+    logits[0, 1, 30] = 0.0
+    logits[0, 1, 10] = -0.0                 # -0 first: 10, although +0 orders above -0 bitwise
+    logits[0, 1, 15000] = -0.0
+    logits[0, 2, :] = float("-inf")         # all -inf: 0
+    logits[0, 3, :] = float("-inf")
+    logits[0, 3, V - 3] = -1.0              # one finite value among -inf
+    logits[1, 4, 12000] = float("inf")
+    logits[1, 4, 11999] = float("inf")      # tied +inf: 11999
+    post_ref = torch.argmax(logits.float(), dim=-1)
+    post, _, _ = r.verify_accept(logits, verify)
+    assert r.status() == 0
+    assert torch.equal(post, post_ref)
+    assert post[0, 0] == 50 and post[0, 1] == 10 and post[0, 2] == 0 and post[0, 3] == V - 3
+    assert post[1, 4] == 11999
+    assert np.array_equal(post.cpu().numpy(), np.argmax(logits.float().cpu().numpy(), axis=-1))
+    r.close()
+
+
+@pytest.mark.parametrize("B,K1", [(1, 1), (1, 16), (3, 5), (32, 64)])
+def test_verify_accept_grid_shapes_full_vocab(B, K1):
+    """The vocab of a row is cut into as many chunks as one wave of CTAs
+    allows: from 1 row (many chunks) to 32 x 64 rows (one chunk per row)."""
+    V = 151936
+    r = _runner(B, V)
+    logits, verify, post_ref = _case(B, K1, V, torch.bfloat16, 13 + B + K1)
+    logits[0, K1 - 1, V - 1] = 40.0         # maximum at the last entry of a row
+    post_ref = torch.argmax(logits.float(), dim=-1)
+    post, acc, bonus = r.verify_accept(logits, verify)
+    assert r.status() == 0
+    assert torch.equal(post, post_ref)
+    ea, eb = O.accept(verify.cpu().numpy(), post_ref.cpu().numpy())
+    assert np.array_equal(acc.cpu().numpy(), ea)
+    assert np.array_equal(bonus.cpu().numpy(), eb)
+    r.close()
