@@ -94,6 +94,9 @@ struct dd_handle {
   int ctas_per_sm_big = 2;
   int ctas_per_sm_small = 2;
   int max_nacc = 1;               // DD_NACC
+  int wide_two_per_sm = 1;        // DD_WIDE_TWO_PER_SM: passes of 64 < N <= 128 run two CTAs per SM
+  int wide_epi_warps = 8;         // DD_WIDE_EPI_WARPS: epilogue warps of z / lm_head / table passes with N > 128
+  int wide_pair = 0;              // DD_WIDE_PAIR: those passes as CTA pairs (M = 256 tiles, cta_group::2)
   int tmem_cols_per_cta = 128;    // DD_TMEM_COLS
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
   // Vocab sharding (dd_set_vocab_shard): this rank owns vocab rows
@@ -242,13 +245,13 @@ int timing_end(dd_handle* h, cudaStream_t st) {
 
 // Opt the gemv kernel into the full 227 KB of dynamic shared memory, once
 // per (device, element type).
-template <typename T, int kPhase>
+template <typename T, int kPhase, int kEpiWarps = 4, bool kPair = false>
 int set_kernel_attrs(dd_handle* h) {
   static bool done[64] = {};
   const int d = h->device & 63;
   if (!done[d]) {
-    DD_CUDA(h, cudaFuncSetAttribute(gemv_stream_kernel<T, kPhase>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    227 * 1024));
+    DD_CUDA(h, cudaFuncSetAttribute(gemv_stream_kernel<T, kPhase, kEpiWarps, kPair>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     done[d] = true;
   }
   return DD_OK;
@@ -259,8 +262,9 @@ int set_kernel_attrs(dd_handle* h) {
 // the kernels).
 struct Launch {
   cudaLaunchConfig_t cfg{};
-  cudaLaunchAttribute attr[1];
-  Launch(dim3 grid, dim3 block, size_t smem, cudaStream_t st) {
+  cudaLaunchAttribute attr[2];
+  // cluster_x > 1: clusters of cluster_x CTAs along x (CTA pairs).
+  Launch(dim3 grid, dim3 block, size_t smem, cudaStream_t st, unsigned cluster_x = 1) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = grid;
@@ -269,8 +273,21 @@ struct Launch {
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (cluster_x > 1) {
+      attr[1].id = cudaLaunchAttributeClusterDimension;
+      attr[1].val.clusterDim.x = cluster_x;
+      attr[1].val.clusterDim.y = 1;
+      attr[1].val.clusterDim.z = 1;
+      cfg.numAttrs = 2;
+    }
   }
 };
+
+// Whether a z / lm_head / table pass of N X rows runs as CTA pairs; its
+// caller then encodes the X map with boxes of N / 2 rows (GemvParams::b_box_rows).
+bool wide_pair_pass(const dd_handle* h, int n) {
+  return h->wide_pair && h->wide_epi_warps == 8 && n > 128 && !h->pack;
+}
 
 // Fill the pass-independent launch fields of a gemv phase and launch it.
 template <typename T, int kPhase>
@@ -283,16 +300,32 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
     tiles += p.seg[s].tiles;
   }
   if (tiles > h->max_tiles) return fail(h, DD_EINVAL, "phase has %d tiles > %d", tiles, h->max_tiles);
-  p.units = (long long)tiles * p.KC;
-  p.b_bytes = (uint32_t)p.N * 128u;
+  constexpr bool kXRowMajor = kPhase == PH_ZLM || kPhase == PH_Z || kPhase == PH_TABLE;
+  // CTA pairs: the caller encoded the X map with half-height boxes.
+  const bool pair = kXRowMajor && p.b_box_rows > 0 && 2 * p.b_box_rows == p.N && wide_pair_pass(h, p.N) &&
+                    !p.packed[0] && !p.packed[1];
+  if (!pair) p.b_box_rows = p.N;
+  p.tiles128 = tiles;
+  p.units = (long long)(pair ? (tiles + 1) / 2 : tiles) * p.KC;
+  p.b_bytes = (uint32_t)p.b_box_rows * 128u;
   p.stage_bytes = kATileBytes + p.b_bytes;
+  // Wide passes (N > 64) take one CTA per SM with a 196 KB ring, except that
+  // up to N = 128 three stages of at most 32 KB and 2 x 128 TMEM columns
+  // leave room for a second CTA on the SM.  Narrower passes: the class ring.
+  const bool wide2 = p.N > 64 && p.N <= 128 && h->wide_two_per_sm;
   const uint32_t ring_budget =
-      p.N > 64 ? 196u * 1024u : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
+      p.N > 64 ? (wide2 ? 3u * p.stage_bytes : 196u * 1024u)
+               : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
   // At least four stages, three when the base-logit buffers take the room
   // of the fourth (batch 32), so that two CTAs still share an SM.
-  p.stages = std::max(p.base_stage_bytes ? 3 : 4, std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
-  p.l2_prefetch_units = (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
-  p.xpose_bytes = (kPhase == PH_ZLM || kPhase == PH_Z || kPhase == PH_TABLE) ? kXposeBytes : 0u;
+  p.stages = std::max(p.base_stage_bytes || wide2 ? 3 : 4,
+                      std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  p.l2_prefetch_units = pair ? 0 : (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
+  // X-row-major outputs (z, base logits, the table): a staging area per
+  // epilogue warpgroup; passes wider than 128 columns (one CTA per SM) get two
+  // warpgroups.
+  const bool epi8 = kXRowMajor && p.N > 128 && h->wide_epi_warps == 8;
+  p.xpose_bytes = kXRowMajor ? (epi8 ? 2u : 1u) * kXposeBytes : 0u;
   const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes + 2 * p.base_stage_bytes;
   if ((size_t)p.stages * p.stage_bytes + fixed > 227 * 1024) p.stages = (227 * 1024 - fixed) / p.stage_bytes;
   p.acc_slots = 2;  // the epilogue of one tile overlaps the next tile's MMAs (2 x 256 columns at most)
@@ -303,7 +336,8 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   uint32_t cols = 32;
   while (cols < (uint32_t)(p.acc_slots * p.nacc * p.N)) cols <<= 1;
   p.tmem_cols = cols;
-  p.idesc = idesc_f16((uint32_t)p.N, std::is_same<T, __half>::value ? 0u : 1u);
+  p.idesc = pair ? idesc_f16_m256((uint32_t)p.N, std::is_same<T, __half>::value ? 0u : 1u)
+               : idesc_f16((uint32_t)p.N, std::is_same<T, __half>::value ? 0u : 1u);
   p.partials = h->partials;
   p.tile_counters = h->counters;
   p.status = h->status;
@@ -333,7 +367,31 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
     if (2LL * tiles * k >= slots) grid = (int)(tiles * k);
   }
   if (grid < 1) grid = 1;
-  int rc = set_kernel_attrs<T, kPhase>(h);
+  int rc = DD_OK;
+  if constexpr (kXRowMajor) {
+    if (pair) {  // clusters of 2 on the pair-tile partition
+      const long long pair_slots = (long long)h->num_sms / 2;
+      const long long pairs = std::max<long long>(
+          1, std::min<long long>(pair_slots, allow_split ? p.units / h->min_units_per_cta : (tiles + 1) / 2));
+      rc = set_kernel_attrs<T, kPhase, 8, true>(h);
+      if (rc) return rc;
+      rc = timing_begin(h, kPhase, st);
+      if (rc) return rc;
+      Launch L(dim3((unsigned)(2 * pairs)), dim3((kEpiWarp0 + 8) * 32), smem, st, 2);
+      DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, gemv_stream_kernel<T, kPhase, 8, true>, a0, a1 ? *a1 : a0, b, p));
+      return timing_end(h, st);
+    }
+    if (epi8) {
+      rc = set_kernel_attrs<T, kPhase, 8>(h);
+      if (rc) return rc;
+      rc = timing_begin(h, kPhase, st);
+      if (rc) return rc;
+      Launch L(dim3(grid), dim3((kEpiWarp0 + 8) * 32), smem, st);
+      DD_CUDA(h, cudaLaunchKernelEx(&L.cfg, gemv_stream_kernel<T, kPhase, 8>, a0, a1 ? *a1 : a0, b, p));
+      return timing_end(h, st);
+    }
+  }
+  rc = set_kernel_attrs<T, kPhase>(h);
   if (rc) return rc;
   rc = timing_begin(h, kPhase, st);
   if (rc) return rc;
@@ -503,9 +561,10 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
   const int rows = c.batch * positions;
   CUtensorMap tm_x;
   const int n_pass = std::min(256, round_up(rows, 16));
+  const int x_box = wide_pair_pass(h, n_pass) ? n_pass / 2 : n_pass;  // CTA pairs load half the rows each
   int rc = DD_OK;
   if constexpr (!std::is_same<T, float>::value) {
-    rc = encode_kmajor(h, &tm_x, ph, c.dtype, c.hidden, rows, c.hidden, n_pass);
+    rc = encode_kmajor(h, &tm_x, ph, c.dtype, c.hidden, rows, c.hidden, x_box);
     if (rc) return rc;
   }
   for (int n_off = 0; n_off < rows; n_off += 256) {
@@ -517,7 +576,8 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
     p.w32[1] = static_cast<const float*>(h->w.fc1);
     p.w32_ld[1] = h->w.fc1_ld;
     const int n_valid = std::min(256, rows - n_off);
-    p.N = n_pass;  // == the TMA box height, so expect_tx matches the bytes every load delivers
+    p.N = n_pass;  // the TMA box height (x_box: N, or N / 2 per CTA of a pair), so expect_tx matches the loads
+    p.b_box_rows = x_box;
     p.n_off = n_off;
     p.n_valid = n_valid;
     p.K = c.hidden;
@@ -942,7 +1002,8 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
-// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE) over the defaults of a fresh
+// DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE,
+// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -966,6 +1027,9 @@ void read_launch_env(dd_handle* h) {
   h->l2_prefetch_kb = env_int("DD_L2_PREFETCH_KB", d.l2_prefetch_kb, 0, 4096);
   h->fuse_cell = env_int("DD_FUSE_CELL", d.fuse_cell, 0, 1);
   h->base_stage = env_int("DD_BASE_STAGE", d.base_stage, 0, 1);
+  h->wide_two_per_sm = env_int("DD_WIDE_TWO_PER_SM", d.wide_two_per_sm, 0, 1);
+  h->wide_epi_warps = env_int("DD_WIDE_EPI_WARPS", d.wide_epi_warps, 4, 8) == 8 ? 8 : 4;
+  h->wide_pair = env_int("DD_WIDE_PAIR", d.wide_pair, 0, 1);
 }
 
 }  // namespace
@@ -979,6 +1043,8 @@ template <typename T>
 static int launch_verify(dd_handle* h, const T* logits, int dt, int32_t k1, const int64_t* verify_ids,
                          int64_t* posterior_out, int32_t* accept_out, int64_t* bonus_out, void* stream) {
   const dd_config& c = h->cfg;
+  const long long rows = (long long)c.batch * k1;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (!h->verify_per_sm[dt]) {
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, verify_accept_kernel<T>, kVerifyThreads, 0) !=
@@ -988,17 +1054,15 @@ static int launch_verify(dd_handle* h, const T* logits, int dt, int32_t k1, cons
     h->verify_per_sm[dt] = per_sm;
   }
   constexpr int kVec = 16 / (int)sizeof(T);
-  const long long rows = (long long)c.batch * k1;
   const long long slots = (long long)h->num_sms * h->verify_per_sm[dt];
   const int min_chunk = kVerifyThreads * kVerifyGroup * kVec;
   int parts = (int)std::max<long long>(1, slots / rows);
   parts = std::min(parts, std::max(1, c.vocab / min_chunk));
   const int chunk = ceil_div(ceil_div(c.vocab, parts), kVec) * kVec;
-  Launch launch(dim3(ceil_div(c.vocab, chunk), (unsigned)rows), dim3(kVerifyThreads), 0,
-           reinterpret_cast<cudaStream_t>(stream));
-  const cudaError_t e = cudaLaunchKernelEx(&launch.cfg, verify_accept_kernel<T>, logits, c.vocab, chunk, c.batch, (int)k1,
-                                           verify_ids, posterior_out, accept_out, bonus_out, h->vwords, h->vdone,
-                                           h->status);
+  Launch launch(dim3(ceil_div(c.vocab, chunk), (unsigned)rows), dim3(kVerifyThreads), 0, st);
+  const cudaError_t e = cudaLaunchKernelEx(&launch.cfg, verify_accept_kernel<T>, logits, c.vocab, chunk, c.batch,
+                                           (int)k1, verify_ids, posterior_out, accept_out, bonus_out, h->vwords,
+                                           h->vdone, h->status);
   if (e != cudaSuccess) return fail(h, DD_ECUDA, "verify_accept launch: %s", cudaGetErrorString(e));
   return DD_OK;
 }
@@ -1193,7 +1257,7 @@ int dd_build_table(dd_handle* h, const void* embed, int64_t embed_ld, const void
       return fail(h, DD_EINVAL, "fp32 embed / w_ih must be 16-byte aligned with row strides a multiple of 4");
   } else {
     rc = encode_kmajor(h, &tm_wih, w_ih, c.dtype, c.hidden, 3LL * c.gru_hidden, w_ih_ld, kTileM);
-    if (!rc) rc = encode_kmajor(h, &tm_emb, embed, c.dtype, c.hidden, c.vocab, embed_ld, 256);
+    if (!rc) rc = encode_kmajor(h, &tm_emb, embed, c.dtype, c.hidden, c.vocab, embed_ld, wide_pair_pass(h, 256) ? 128 : 256);
     if (rc) return rc;
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -1203,6 +1267,7 @@ int dd_build_table(dd_handle* h, const void* embed, int64_t embed_ld, const void
     p.seg[0] = {3 * c.gru_hidden, 0, EPI_TABLE};
     p.K = c.hidden;
     p.N = 256;
+    p.b_box_rows = wide_pair_pass(h, 256) ? 128 : 256;
     p.n_off = n_off;
     p.n_valid = std::min(256, c.vocab - n_off);
     p.table_out = table_out;

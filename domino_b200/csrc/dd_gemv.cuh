@@ -80,7 +80,9 @@ struct GemvParams {
   int N;             // MMA N: X rows per pass, multiple of 16, <= 256
   int n_off;         // first X row of this pass
   int n_valid;       // X rows of this pass that carry data (<= N)
-  long long units;   // (tile, k-chunk) units in this pass
+  long long units;   // (tile, k-chunk) units in this pass; CTA pairs: (256-row pair tile, k-chunk)
+  long long tiles128;  // CTA pairs: the 128-row tiles of all segments (a pair tile past them is empty)
+  int b_box_rows;    // rows of tmB's box: N, or N / 2 when the caller encoded it for CTA pairs
   int stages;
   // PH_FC2 with more than four batch rows: the producer also loads each tile's
   // base logits [B, 128] by TMA (the tensor map in tmA1) into one of two
@@ -242,6 +244,8 @@ struct AccView {
   long long row0 = 0;        // global row of the tile's first row
   long long row_end = 0;     // end of the segment's rows (exclusive, global)
   const void* bsm = nullptr; // PH_FC2 staging: this tile's base logits [B][128] in shared memory, or null
+  int grp = 0, ngroups = 1;  // X-row-major outputs: this warpgroup takes 16-column chunks grp, grp + ngroups, ...
+  int pmul = 1, padd = 0;    // partial scratch slot = partial_slot(...) * pmul + padd (CTA pairs: 2, rank)
 };
 
 // Four consecutive elements (8 or 16 bytes, aligned) from shared to global memory.
@@ -284,7 +288,7 @@ __device__ __forceinline__ void acc_chunk(const AccView& a, int ch, float* v) {
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] += t[j];
     } else {
-      const int slot = partial_slot(a.c_lo + s, a.T, a.U, a.G, a.KC);
+      const int slot = partial_slot(a.c_lo + s, a.T, a.U, a.G, a.KC) * a.pmul + a.padd;
       const float* src = a.partials + (size_t)slot * a.N * kTileM;
 #pragma unroll
       for (int j = 0; j < 16; ++j) v[j] += __ldcg(src + (size_t)(ch * 16 + j) * kTileM + a.r);
@@ -391,8 +395,8 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
     // touches each column's page once instead of four times.
     const bool xp = a.xpose != nullptr && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & (4 * sizeof(T) - 1)) == 0;
     T* S = reinterpret_cast<T*>(a.xpose);
-    const int w4 = ept >> 5;
-    for (int ch = 0; ch < nchunks; ++ch) {
+    const int w4 = (ept & 127) >> 5;  // warp within the warpgroup
+    for (int ch = a.grp; ch < nchunks; ch += a.ngroups) {
       float v[16];
       acc_chunk(a, ch, v);
       T vals[16];
@@ -579,13 +583,13 @@ __device__ __forceinline__ void epilogue_tile(const GemvParams& p, const AccView
   }
 }
 
-// Called by the 128 epilogue threads of every CTA once all of its tiles are
-// finished.  The last CTA of the grid to get here sees every argmax word of
-// the launch (atomicMax, fenced) and copies them to every rank's exchange
+// Called by the nthreads epilogue threads of every CTA once all of its tiles
+// are finished.  The last CTA of the grid to get here sees every argmax word
+// of the launch (atomicMax, fenced) and copies them to every rank's exchange
 // buffer, then raises the flags.
-__device__ __forceinline__ void publish_words(const GemvParams& p, int ept, volatile int* flag) {
+__device__ __forceinline__ void publish_words(const GemvParams& p, int ept, volatile int* flag, int nthreads = 128) {
   const Exchange& x = p.xchg;
-  named_bar_sync(1, 128);
+  named_bar_sync(1, nthreads);
   if (ept == 0) {
     __threadfence();
     const unsigned int old = atomicAdd(x.done + p.xslot0, 1u);
@@ -596,13 +600,13 @@ __device__ __forceinline__ void publish_words(const GemvParams& p, int ept, vola
     }
     *flag = last;
   }
-  named_bar_sync(1, 128);
+  named_bar_sync(1, nthreads);
   if (!*flag) return;
   const unsigned long long seq = *x.seq;
   const int par = (int)(seq & 1ull);
   const int nsl = p.xslot1 - p.xslot0;
   const int n = x.world * nsl * x.B;
-  for (int i = ept; i < n; i += 128) {
+  for (int i = ept; i < n; i += nthreads) {
     const int j = i / (nsl * x.B);
     const int rem = i - j * nsl * x.B;
     const int slot = p.xslot0 + rem / x.B;
@@ -611,8 +615,8 @@ __device__ __forceinline__ void publish_words(const GemvParams& p, int ept, vola
     __stcg(x.peer[j] + xchg_word(x, par, slot, x.rank, b), w);
   }
   __threadfence_system();
-  named_bar_sync(1, 128);
-  for (int i = ept; i < x.world * nsl; i += 128) {
+  named_bar_sync(1, nthreads);
+  for (int i = ept; i < x.world * nsl; i += nthreads) {
     const int j = i / nsl;
     const int slot = p.xslot0 + (i - j * nsl);
     unsigned long long* f = x.peer[j] + xchg_flag(x, par, slot, x.rank);
@@ -679,10 +683,24 @@ __device__ __forceinline__ void publish_slices_done(const GemvParams& p, int ept
   }
 }
 
-template <typename T, int kPhase>
-__global__ void __launch_bounds__(kThreads, 2)
+// kEpiWarps = 8 (wide z / lm_head / table passes, one CTA per SM): two
+// warpgroups read the accumulator's lane quadrants and split each tile's
+// 16-column chunks between them.
+// kPair (with kEpiWarps = 8): CTA pairs (clusters of 2) share each M = 256
+// weight tile.  Each CTA loads its own 128 weight rows and half of the X rows;
+// rank 0 issues the pair MMAs (cta_group::2) into both CTAs' TMEM and its
+// commits release both CTAs' ring stages and accumulator slots; each CTA's
+// epilogue finishes its own 128 rows, as a lone CTA does.  The pair reads X
+// from shared memory once for both CTAs' rows.
+template <typename T, int kPhase, int kEpiWarps = 4, bool kPair = false>
+__global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ? 2 : 1)
     gemv_stream_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                        const __grid_constant__ CUtensorMap tmB, const GemvParams p) {
+  static_assert(kEpiWarps == 4 || (kEpiWarps == 8 && (kPhase == PH_ZLM || kPhase == PH_Z || kPhase == PH_TABLE)),
+                "two epilogue warpgroups only for the X-row-major output phases");
+  static_assert(!kPair || kEpiWarps == 8, "CTA pairs run the wide passes only");
+  constexpr int kEpiThreads = kEpiWarps * 32;
+  constexpr int kGroups = kEpiWarps / 4;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
@@ -709,8 +727,10 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int G = gridDim.x;
-  const int c = blockIdx.x;
+  // CTA pairs: the pair is the unit of the stream-K partition (c of G).
+  const int rank = kPair ? (int)(blockIdx.x & 1u) : 0;
+  const int G = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  const int c = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
   const long long U = p.units;
   const long long u_begin = unit_begin(c, U, G);
   const long long u_end = unit_begin(c + 1, U, G);
@@ -723,7 +743,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&accf[s], 1);
-      mbar_init(&acce[s], 128);
+      mbar_init(&acce[s], kPair ? 2 * kEpiThreads : kEpiThreads);  // pairs: both CTAs' epilogues, on rank 0
     }
     mbar_init(drain, 1);
     for (int s = 0; s < 2; ++s) {
@@ -744,11 +764,19 @@ __global__ void __launch_bounds__(kThreads, 2)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, p.tmem_cols);
-    tmem_relinquish();
+    if constexpr (kPair) {
+      tmem_alloc_pair(tmem_holder, p.tmem_cols);  // warp 1 of both CTAs, together
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, p.tmem_cols);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (kPair)
+    cluster_sync_all();  // both CTAs' barriers exist before either signals the other's
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -766,6 +794,21 @@ __global__ void __launch_bounds__(kThreads, 2)
       // Unit u of this CTA's range is (tile, kc) = (u / KC, u % KC); the
       // loops below advance (tile, kc) and the ring position incrementally.
       auto load_a = [&](int stage, long long tile, int kc) {
+        if constexpr (kPair) {
+          const long long t128 = 2 * tile + rank;  // this CTA's 128 rows of the pair tile
+          const uint32_t bar0 = smem_in_cta(&full[stage], 0);
+          if (t128 >= p.tiles128) {  // past the last tile: a box of zeros (rows past segment 0's end)
+            tma_load_2d_pair(ring + (size_t)stage * p.stage_bytes, &tmA0, bar0, kc * kChunkK,
+                             (int)((p.seg[0].row_off / kTileM + p.seg[0].tiles) * kTileM), pol_w);
+            return;
+          }
+          const bool s1 = t128 >= p.seg[0].tiles;
+          const GemvSeg& sg = p.seg[s1 ? 1 : 0];
+          const long long w_tile = (s1 ? t128 - p.seg[0].tiles : t128) + sg.row_off / kTileM;
+          tma_load_2d_pair(ring + (size_t)stage * p.stage_bytes, s1 ? &tmA1 : &tmA0, bar0, kc * kChunkK,
+                           (int)(w_tile * kTileM), pol_w);
+          return;
+        }
         const bool s1 = tile >= p.seg[0].tiles;
         const GemvSeg& sg = p.seg[s1 ? 1 : 0];
         const long long w_tile = (s1 ? tile - p.seg[0].tiles : tile) + sg.row_off / kTileM;
@@ -779,8 +822,21 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
       };
       auto load_b = [&](int stage, int kc) {
-        tma_load_2d(ring + (size_t)stage * p.stage_bytes + kATileBytes, &tmB, &full[stage], kc * kChunkK, p.n_off,
-                    pol_x);
+        if constexpr (kPair)  // this CTA's half of the pass's X rows
+          tma_load_2d_pair(ring + (size_t)stage * p.stage_bytes + kATileBytes, &tmB, smem_in_cta(&full[stage], 0),
+                           kc * kChunkK, p.n_off + rank * p.b_box_rows, pol_x);
+        else
+          tma_load_2d(ring + (size_t)stage * p.stage_bytes + kATileBytes, &tmB, &full[stage], kc * kChunkK, p.n_off,
+                      pol_x);
+      };
+      // The bytes a stage's full barrier waits for: pairs count both CTAs'
+      // loads on rank 0's barrier, and only rank 0 posts them.
+      auto expect_stage = [&](int stage) {
+        if constexpr (kPair) {
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (kATileBytes + p.b_bytes));
+        } else {
+          mbar_arrive_expect_tx(&full[stage], kATileBytes + p.b_bytes);
+        }
       };
       const long long tile_begin = u_begin / KC;
       const int kc_begin = (int)(u_begin - tile_begin * KC);
@@ -788,7 +844,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       int kc = kc_begin;
       // Weights first: they do not depend on the previous kernel.
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], kATileBytes + p.b_bytes);
+        expect_stage(i);
         load_a(i, tile, kc);
         if (++kc == KC) {
           kc = 0;
@@ -849,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (; ok && it < n_my; ++it) {
         if (!base_upto(tile)) break;
         if (!mbar_wait_bounded(&empty[stage], parity ^ 1u, abort_flag)) break;
-        mbar_arrive_expect_tx(&full[stage], kATileBytes + p.b_bytes);
+        expect_stage(stage);
         load_a(stage, tile, kc);
         load_b(stage, kc);
         if (++kc == KC) {
@@ -865,7 +921,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else if (warp == 1) {
     pdl_wait_primary();
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       // ------------------------------------------------ MMA issuer
       long long u = u_begin;
       long long it = 0;
@@ -898,16 +954,29 @@ __global__ void __launch_bounds__(kThreads, 2)
           for (int k = 0; k < kChunkK / 16; ++k) {
             const int ks = (kc - kc0) * (kChunkK / 16) + k;
             const int acc = ks % p.nacc;
-            mma_f16_ss(d + (uint32_t)(acc * p.N), adesc + 2 * k, bdesc + 2 * k, p.idesc, ks >= p.nacc ? 1u : 0u);
+            if constexpr (kPair)
+              mma_f16_ss_pair(d + (uint32_t)(acc * p.N), adesc + 2 * k, bdesc + 2 * k, p.idesc, ks >= p.nacc ? 1u : 0u);
+            else
+              mma_f16_ss(d + (uint32_t)(acc * p.N), adesc + 2 * k, bdesc + 2 * k, p.idesc, ks >= p.nacc ? 1u : 0u);
           }
-          mma_commit(&empty[stage]);
+          if constexpr (kPair) {  // the stage is free in both CTAs
+            mma_commit_pair(smem_in_cta(&empty[stage], 0));
+            mma_commit_pair(smem_in_cta(&empty[stage], 1));
+          } else {
+            mma_commit(&empty[stage]);
+          }
           if (++stage == p.stages) {
             stage = 0;
             parity ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(&accf[slot]);
+        if constexpr (kPair) {  // both CTAs' accumulators are ready
+          mma_commit_pair(smem_in_cta(&accf[slot], 0));
+          mma_commit_pair(smem_in_cta(&accf[slot], 1));
+        } else {
+          mma_commit(&accf[slot]);
+        }
         ++acc_it;
         u += kc1 - kc0;
         (void)tile;
@@ -915,9 +984,10 @@ __global__ void __launch_bounds__(kThreads, 2)
       *consumed = it;
     }
   } else {
-    // -------------------------------------------------- epilogue (warps 2..5)
+    // -------------------------------------------------- epilogue (warps 2 .. 2 + kEpiWarps - 1)
     pdl_wait_primary();
-    const int ept = threadIdx.x - kEpiWarp0 * 32;  // 0..127
+    const int ept = threadIdx.x - kEpiWarp0 * 32;  // 0 .. kEpiThreads - 1
+    const int grp = ept >> 7;                       // warpgroup
     const int q = warp & 3;                         // TMEM lane quadrant of this warp
     const int r = q * 32 + lane;                    // row within the tile
     long long u = u_begin;
@@ -930,20 +1000,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int slot = acc_it % p.acc_slots;
       const uint32_t use = (uint32_t)(acc_it / p.acc_slots);
       const bool got = mbar_wait_bounded(&accf[slot], use & 1u, abort_flag);
-      if (!named_bar_and(1, 128, got)) break;
+      if (!named_bar_and(1, kEpiThreads, got)) break;
       tc_fence_after();
 
-      const bool s1 = tile >= p.seg[0].tiles;
+      // The 128-row tile this CTA finishes (pairs: its half of the pair tile).
+      const long long t128 = kPair ? 2 * tile + rank : tile;
+      if (kPair && t128 >= p.tiles128) {  // the empty half of a last pair tile: nothing to finish
+        tc_fence_before();
+        mbar_arrive_cluster(smem_in_cta(&acce[slot], 0));
+        ++acc_it;
+        u += kc1 - kc0;
+        continue;
+      }
+      const bool s1 = t128 >= p.seg[0].tiles;
       const GemvSeg& sg = p.seg[s1 ? 1 : 0];
-      const int local_row = (int)((s1 ? tile - p.seg[0].tiles : tile) * kTileM) + r;
+      const int local_row = (int)((s1 ? t128 - p.seg[0].tiles : t128) * kTileM) + r;
       const bool valid = local_row < sg.rows;
       const int row = sg.row_off + local_row;
 
       AccView a;
       a.taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(slot * p.N * p.nacc);
       a.nacc = p.nacc;
-      a.bar = 1;
-      a.xpose = p.xpose_bytes ? tail + kSmemTail : nullptr;
+      a.bar = kGroups > 1 ? 2 + grp : 1;
+      a.xpose = p.xpose_bytes ? tail + kSmemTail + (size_t)grp * kXposeBytes : nullptr;
+      a.grp = grp;
+      a.ngroups = kGroups;
       a.row0 = row - r;
       a.row_end = (long long)sg.row_off + sg.rows;
       a.combine = false;
@@ -958,6 +1039,8 @@ __global__ void __launch_bounds__(kThreads, 2)
       a.G = G;
       a.KC = KC;
       a.bsm = nullptr;
+      a.pmul = kPair ? 2 : 1;
+      a.padd = rank;
       int bslot = 0;
       if constexpr (kPhase == PH_FC2) {
         if (p.base_stage_bytes) {
@@ -965,7 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           const long long n = tile - u_begin / KC;
           bslot = (int)(n & 1);
           const bool landed = mbar_wait_bounded(&bfull[bslot], (uint32_t)((n >> 1) & 1), abort_flag);
-          if (!named_bar_and(1, 128, landed)) break;
+          if (!named_bar_and(1, kEpiThreads, landed)) break;
           if (ept == 0) *bconsumed = n + 1;
           a.bsm = bstage + (size_t)bslot * p.base_stage_bytes;
         }
@@ -979,25 +1062,25 @@ __global__ void __launch_bounds__(kThreads, 2)
         a.nseg = c_hi - c_lo + 1;
         a.myseg = c - c_lo;
         a.c_lo = c_lo;
-        float* mine = p.partials + (size_t)partial_slot(c, tile, U, G, KC) * p.N * kTileM;
-        for (int ch = 0; ch < p.N / 16; ++ch) {
+        float* mine = p.partials + (size_t)(partial_slot(c, tile, U, G, KC) * a.pmul + a.padd) * p.N * kTileM;
+        for (int ch = grp; ch < p.N / 16; ch += kGroups) {
           float v[16];
           acc_local(a, ch, v);
 #pragma unroll
           for (int j = 0; j < 16; ++j) __stcg(mine + (size_t)(ch * 16 + j) * kTileM + r, v[j]);
         }
         __threadfence();
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         if (ept == 0) {
-          const unsigned int old = atomicAdd(p.tile_counters + tile, 1u);
+          const unsigned int old = atomicAdd(p.tile_counters + t128, 1u);
           const int last = (old == (unsigned int)(a.nseg - 1)) ? 1 : 0;
           if (last) {
-            p.tile_counters[tile] = 0u;  // ready for the next phase
+            p.tile_counters[t128] = 0u;  // ready for the next phase
             __threadfence();
           }
           *fin_flag = last;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         finish = *fin_flag != 0;
         if (finish) {
           __threadfence();
@@ -1007,24 +1090,27 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (finish) epilogue_tile<T, kPhase>(p, a, sg.kind, row, valid, q, lane, red, ept);
       if constexpr (kPhase == PH_FC2) {
         if (p.base_stage_bytes) {
-          named_bar_sync(1, 128);  // all reads of this base buffer done
+          named_bar_sync(1, kEpiThreads);  // all reads of this base buffer done
           if (ept == 0) mbar_arrive(&bempty[bslot]);
         }
       }
 
       tc_fence_before();
-      mbar_arrive(&acce[slot]);
+      if constexpr (kPair)
+        mbar_arrive_cluster(smem_in_cta(&acce[slot], 0));  // rank 0's MMA issuer waits for both CTAs
+      else
+        mbar_arrive(&acce[slot]);
       ++acc_it;
       u += kc1 - kc0;
     }
     if constexpr (kPhase == PH_FC2 || kPhase == PH_ZLM) {
       // All 128 threads decide together whether to publish (publish_words
       // contains named barriers).
-      if (p.xchg.world > 1 && p.xslot1 > p.xslot0 && named_bar_and(1, 128, *abort_flag == 0))
-        publish_words(p, ept, fin_flag);
+      if (p.xchg.world > 1 && p.xslot1 > p.xslot0 && named_bar_and(1, kEpiThreads, *abort_flag == 0))
+        publish_words(p, ept, fin_flag, kEpiThreads);
     }
     if constexpr (kPhase == PH_SGH) {
-      if (p.xchg.world > 1 && p.sflag_slot >= 0 && named_bar_and(1, 128, *abort_flag == 0))
+      if (p.xchg.world > 1 && p.sflag_slot >= 0 && named_bar_and(1, kEpiThreads, *abort_flag == 0))
         publish_slices_done(p, ept, fin_flag);
     }
     if constexpr (kPhase == PH_FC2) {
@@ -1032,14 +1118,14 @@ __global__ void __launch_bounds__(kThreads, 2)
         // Every CTA's argmax words are final once all have arrived; then each
         // CTA runs its share of the GRU step (a CTA that gave up arrives
         // without waiting, so that the others are not held).
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         if (ept == 0) {
           const bool aborted = *abort_flag != 0;
           const bool ok = grid_barrier(p.gbar, gridDim.x, !aborted);
           if (!ok) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
           *fin_flag = ok && !aborted;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kEpiThreads);
         if (*fin_flag) {
           const int n = p.cell.B * (p.cell.G / 8);
           for (int idx = c * 128 + ept; idx < n; idx += G * 128) cell_apply<T>(p.cell, idx);
@@ -1049,26 +1135,53 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   __syncthreads();
-  if (*abort_flag) {
-    // Unwind after a timed-out wait: let in-flight MMAs and TMA loads land
-    // before the shared memory and TMEM are released.
-    if (warp == 1 && lane == 0) {
-      mma_commit(drain);
+  if constexpr (kPair) {
+    // Rank 0's MMAs read both CTAs' shared memory and write both CTAs' TMEM,
+    // and both epilogues arrive on rank 0's barriers: neither CTA releases
+    // anything before the other is done.
+    if (*abort_flag && rank == 0 && warp == 1 && lane == 0) {
+      mma_commit_pair(smem_in_cta(drain, 0));
       wait_ns(drain, 0, 100ull * 1000 * 1000);
     }
-    if (warp == 0 && lane == 0) {
-      for (long long it = *consumed; it < *issued; ++it)
-        wait_ns(&full[it % p.stages], (uint32_t)((it / p.stages) & 1), 100ull * 1000 * 1000);
-      for (long long n = *bconsumed; n < *bissued; ++n)
-        wait_ns(&bfull[n & 1], (uint32_t)((n >> 1) & 1), 100ull * 1000 * 1000);
+    cluster_sync_all();
+    // After a timed-out wait in either CTA: both CTAs' loads count on rank
+    // 0's full barriers, so rank 0 lets every stage either CTA issued land.
+    if (rank == 0 && warp == 0 && lane == 0) {
+      const bool peer_abort = ld_cluster_u32(smem_in_cta((const void*)abort_flag, 1)) != 0;
+      if (*abort_flag || peer_abort) {
+        const long long peer_issued = ld_cluster_s64(smem_in_cta(issued, 1));
+        const long long upto = *issued > peer_issued ? *issued : peer_issued;
+        for (long long it = *consumed; it < upto; ++it)
+          wait_ns(&full[it % p.stages], (uint32_t)((it / p.stages) & 1), 100ull * 1000 * 1000);
+      }
     }
-    if (threadIdx.x == 0) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
-    __syncthreads();
+    if (*abort_flag && threadIdx.x == 0) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
+    cluster_sync_all();
+  } else {
+    if (*abort_flag) {
+      // Unwind after a timed-out wait: let in-flight MMAs and TMA loads land
+      // before the shared memory and TMEM are released.
+      if (warp == 1 && lane == 0) {
+        mma_commit(drain);
+        wait_ns(drain, 0, 100ull * 1000 * 1000);
+      }
+      if (warp == 0 && lane == 0) {
+        for (long long it = *consumed; it < *issued; ++it)
+          wait_ns(&full[it % p.stages], (uint32_t)((it / p.stages) & 1), 100ull * 1000 * 1000);
+        for (long long n = *bconsumed; n < *bissued; ++n)
+          wait_ns(&bfull[n & 1], (uint32_t)((n >> 1) & 1), 100ull * 1000 * 1000);
+      }
+      if (threadIdx.x == 0) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
+      __syncthreads();
+    }
   }
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    if constexpr (kPair)
+      tmem_dealloc_pair(tmem_base, p.tmem_cols);
+    else
+      tmem_dealloc(tmem_base, p.tmem_cols);
   }
 }
 

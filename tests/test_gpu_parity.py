@@ -323,3 +323,41 @@ def test_fused_cell_matches_separate_cell_exactly(B, P, monkeypatch):
     vf, _ = rf.draft_block(last, ph2)
     assert torch.equal(vs, vf)
     assert rs.status() == 0 and rf.status() == 0
+
+
+@pytest.mark.parametrize("B", [6, 20, 32])
+@pytest.mark.parametrize("shape", ["DD_WIDE_PAIR=1", "DD_WIDE_EPI_WARPS=4", "DD_WIDE_TWO_PER_SM=0"])
+def test_wide_pass_launch_shapes(B, shape, monkeypatch):
+    """The z / lm_head pass and the table build under each launch shape of
+    the wide passes: CTA pairs (M = 256 tiles, cta_group::2), one epilogue
+    warpgroup instead of two, one CTA per SM at N <= 128.  The lm_head and
+    W_z rows make an odd number of 128-row tiles, so the last pair tile has
+    an empty half.  Base logits against the oracle's lm_head, tokens by
+    teacher forcing, the table against the default launch shape."""
+    H, G, E, S, P, V = 128, 128, 320, 15, 2, 4741
+    draft, target = random_modules(H, G, E, V, seed=57 + B, fc2_std=0.08)
+    K = P - 1 + S
+    g = torch.Generator().manual_seed(B)
+    ph = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    last = torch.randint(0, V, (B,), generator=g).cuda()
+    ref_runner = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    name, val = shape.split("=")
+    monkeypatch.setenv(name, val)
+    r = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
+    tab, tab_ref = r.table.float(), ref_runner.table.float()
+    assert torch.all((tab - tab_ref).abs() <= TOL + TOL * tab_ref.abs())
+    print(f"{shape} B={B}: table bit-equal to the default launch shape: {torch.equal(r.table, ref_runner.table)}")
+    verify, base = r.draft_block(last, ph)
+    assert r.status() == 0
+    lm = target.lm_head.weight.detach().float().cpu().numpy()
+    base_ref = O.lm_head(ph.float().cpu().numpy(), lm, "bf16")
+    base_np = base.float().cpu().numpy()
+    assert np.all(np.abs(base_np - base_ref) <= TOL + TOL * np.abs(base_ref))
+    v = verify.cpu().numpy()
+    assert np.array_equal(v[:, 1:P], O.pure_draft_prefix(base_np, P - 1))
+    prefix_ids = torch.from_numpy(v[:, :P]).cuda()
+    out = r(prefix_ids, ph[:, P - 1:], base[:, P - 1:])
+    assert torch.equal(out.cpu(), torch.from_numpy(v[:, P:]))
+    teacher_forced_check(oracle_weights(draft, target), prefix_ids, ph[:, P - 1:], base[:, P - 1:], out)
+    r.close()
+    ref_runner.close()

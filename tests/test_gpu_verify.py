@@ -37,7 +37,7 @@ def _case(B, K1, V, dtype, seed):
     return logits, verify, post
 
 
-@pytest.mark.parametrize("V", [5003, 20011])
+@pytest.mark.parametrize("V", [5003, 20011, 20016])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_verify_accept_matches_argmax_and_acceptance(V, dtype):
     B, K1 = 4, 16
@@ -65,12 +65,14 @@ def test_verify_accept_full_vocab_and_full_acceptance():
     r.close()
 
 
+@pytest.mark.parametrize("V", [20011, 20016])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_verify_accept_nan_ranks_first_like_torch_argmax(dtype):
+def test_verify_accept_nan_ranks_first_like_torch_argmax(dtype, V):
     """A NaN logit wins over every number and the first NaN wins, as in
-    torch.argmax (code/dflash.py:472); the odd V leaves rows unaligned, so the
-    scalar head and tail of the vector loop see NaNs too."""
-    B, K1, V = 3, 16, 20011
+    torch.argmax (code/dflash.py:472).  The odd V leaves rows unaligned, so
+    the scalar head and tail of the vector loop see NaNs too; the even V
+    gives 16-byte aligned rows (no scalar head)."""
+    B, K1 = 3, 16
     r = _runner(B, V)
     logits, verify, _ = _case(B, K1, V, dtype, 7)
     logits[0, 2, 9000] = float("nan")
@@ -88,12 +90,13 @@ def test_verify_accept_nan_ranks_first_like_torch_argmax(dtype):
     r.close()
 
 
+@pytest.mark.parametrize("V", [20011, 20016])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-def test_verify_accept_signed_zeros_and_infinities(dtype):
+def test_verify_accept_signed_zeros_and_infinities(dtype, V):
     """-0 and +0 are equal for torch.argmax, so the first zero wins whatever
     its sign; rows of -inf (all, or all but one) and tied +inf maxima keep
     the first index (code/dflash.py:472)."""
-    B, K1, V = 2, 16, 20011
+    B, K1 = 2, 16
     r = _runner(B, V)
     _, verify, _ = _case(B, K1, V, dtype, 11)
     logits = torch.full((B, K1, V), -1.0, device="cuda", dtype=dtype)
@@ -133,3 +136,4 @@ def test_verify_accept_grid_shapes_full_vocab(B, K1):
     assert np.array_equal(acc.cpu().numpy(), ea)
     assert np.array_equal(bonus.cpu().numpy(), eb)
     r.close()
+
