@@ -49,6 +49,8 @@ MODELS = {
     "qwen3.6-27b": dict(H=5120, G=5120, E=17408, V=151936),
 }
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0            # burst; sustained under the power cap ~1400
+FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
 
 
 def parse_args():
@@ -129,6 +131,49 @@ def measured_peak_hbm():
         return float(d["hbm_gbs"]), "measured"
     except Exception:
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_peak_tflops():
+    """(burst, sustained) dense bf16 TFLOP/s of this pool's B200s (cuBLAS), or the fallback."""
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, FALLBACK_BF16_TFLOPS_SUSTAINED, "fallback"
+
+
+def zlm_passes(rows):
+    """X rows per z / lm_head pass and the pass count, as the library splits them
+    (at most 256 per pass, as equal as the 16-row MMA granularity allows)."""
+    passes = -(-rows // 256)
+    per = -(-rows // passes)
+    return -(-per // 16) * 16, passes
+
+
+def measure_cublas_linear(device, n, k, r, iters=10):
+    """cuBLAS (torch F.linear) on the same GEMM as one z / lm_head pass:
+    [n x k] . [k x r]^T, bf16, two weight buffers alternated (each > L2)."""
+    import torch
+    import torch.nn.functional as F
+
+    g = torch.Generator(device=device).manual_seed(11)
+    ws = [torch.randn(r, k, generator=g, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    x = torch.randn(n, k, generator=g, device=device, dtype=torch.bfloat16)
+    for i in range(3):
+        F.linear(x, ws[i % 2])
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for i in range(iters):
+        F.linear(x, ws[i % 2])
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / iters
+    del ws, x
+    torch.cuda.empty_cache()
+    return us
 
 
 def committed_traffic(model, B, H, E):
@@ -432,6 +477,25 @@ def run_ours(args):
         }
         if world == 1:
             line["verify_roofline"] = measure_verify(device, V, peak)
+            # The z / lm_head pass: tensor-bound once its passes are wide; its
+            # FLOPs against the measured cuBLAS peaks and against cuBLAS on
+            # the identical GEMM shape (the same rows per pass).
+            rows = B * K
+            n_pass, passes = zlm_passes(rows)
+            zlm_us = statistics.mean(per_kind.get("zlm", [float("nan")])) * 1e3
+            flops = 2.0 * rows * H * (V_local + E) / passes  # valid rows only
+            burst, sustained, tf_src = measured_peak_tflops()
+            ach = flops / (zlm_us / 1e6) / 1e12
+            cublas_us = measure_cublas_linear(device, n_pass, H, V_local + E)
+            line["zlm_roofline"] = {
+                "bound": "tensor" if n_pass > 64 else "hbm",
+                "kernel": "z / lm_head pass (gemv_stream_kernel PH_ZLM)",
+                "gemm": f"[{n_pass} x {H}] . [{H} x {V_local + E}]", "passes_per_block": passes,
+                "flops_per_launch": flops, "avg_launch_us": round(zlm_us, 1),
+                "achieved": round(ach, 1), "unit": "TFLOP/s", "peak": burst, "peak_source": tf_src,
+                "frac": round(ach / burst, 4), "frac_of_sustained": round(ach / sustained, 4),
+                "cublas_same_gemm_us": round(cublas_us, 1), "cublas_over_ours": round(cublas_us / zlm_us, 3),
+            }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args, draft, target, ph_pool[0], last_pool[0], budget_s=30.0)
         print(json.dumps(line), flush=True)

@@ -560,14 +560,18 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
   const dd_config& c = h->cfg;
   const int rows = c.batch * positions;
   CUtensorMap tm_x;
-  const int n_pass = std::min(256, round_up(rows, 16));
+  // Passes of at most 256 X rows (one MMA's N), as equal as the 16-row MMA
+  // granularity allows: 480 rows as 2 x 240, 272 as 2 x 144 (not 256 + 16,
+  // whose second pass would stream every weight for 16 rows).
+  const int passes = ceil_div(rows, 256);
+  const int n_pass = round_up(ceil_div(rows, passes), 16);
   const int x_box = wide_pair_pass(h, n_pass) ? n_pass / 2 : n_pass;  // CTA pairs load half the rows each
   int rc = DD_OK;
   if constexpr (!std::is_same<T, float>::value) {
     rc = encode_kmajor(h, &tm_x, ph, c.dtype, c.hidden, rows, c.hidden, x_box);
     if (rc) return rc;
   }
-  for (int n_off = 0; n_off < rows; n_off += 256) {
+  for (int n_off = 0; n_off < rows; n_off += n_pass) {
     GemvParams p = base_params(h);
     p.x32 = static_cast<const float*>(ph);
     p.x32_ld = c.hidden;
@@ -575,7 +579,7 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
     p.w32_ld[0] = base_out ? h->w.lm_head_ld : h->w.fc1_ld;
     p.w32[1] = static_cast<const float*>(h->w.fc1);
     p.w32_ld[1] = h->w.fc1_ld;
-    const int n_valid = std::min(256, rows - n_off);
+    const int n_valid = std::min(n_pass, rows - n_off);
     p.N = n_pass;  // the TMA box height (x_box: N, or N / 2 per CTA of a pair), so expect_tx matches the loads
     p.b_box_rows = x_box;
     p.n_off = n_off;
@@ -586,7 +590,7 @@ int run_z_phase(dd_handle* h, const void* ph, int positions, int npre, void* bas
     if (base_out) {
       p.nseg = 2;
       p.seg[0] = {h->v_local, 0, EPI_LMHEAD};
-      if (npre > 0 && n_off + 256 >= rows) {  // last pass: the prefix argmax words are final
+      if (npre > 0 && n_off + n_pass >= rows) {  // last pass: the prefix argmax words are final
         p.xslot0 = 0;
         p.xslot1 = npre;
       }
