@@ -485,15 +485,21 @@ def run_ours(args):
             zlm_us = statistics.mean(per_kind.get("zlm", [float("nan")])) * 1e3
             flops = 2.0 * rows * H * (V_local + E) / passes  # valid rows only
             burst, sustained, tf_src = measured_peak_tflops()
-            ach = flops / (zlm_us / 1e6) / 1e12
+            tflops = flops / (zlm_us / 1e6) / 1e12
+            wbytes = (V_local + E) * H * 2 + rows * (H + V_local + E) * 2 / passes  # weights + X + outputs
+            gbs = wbytes / (zlm_us / 1e6) / 1e9
             cublas_us = measure_cublas_linear(device, n_pass, H, V_local + E)
+            tensor = n_pass > 64  # wide passes: the tensor pipe binds; narrow ones stream the weights
             line["zlm_roofline"] = {
-                "bound": "tensor" if n_pass > 64 else "hbm",
+                "bound": "tensor" if tensor else "hbm",
                 "kernel": "z / lm_head pass (gemv_stream_kernel PH_ZLM)",
                 "gemm": f"[{n_pass} x {H}] . [{H} x {V_local + E}]", "passes_per_block": passes,
-                "flops_per_launch": flops, "avg_launch_us": round(zlm_us, 1),
-                "achieved": round(ach, 1), "unit": "TFLOP/s", "peak": burst, "peak_source": tf_src,
-                "frac": round(ach / burst, 4), "frac_of_sustained": round(ach / sustained, 4),
+                "flops_per_launch": flops, "algorithmic_bytes_per_launch": int(wbytes),
+                "avg_launch_us": round(zlm_us, 1), "tflops": round(tflops, 1), "gbs": round(gbs, 1),
+                "achieved": round(tflops if tensor else gbs, 1), "unit": "TFLOP/s" if tensor else "GB/s",
+                "peak": burst if tensor else peak, "peak_source": tf_src if tensor else peak_src,
+                "frac": round(tflops / burst if tensor else gbs / peak, 4),
+                "frac_of_sustained_tflops": round(tflops / sustained, 4),
                 "cublas_same_gemm_us": round(cublas_us, 1), "cublas_over_ours": round(cublas_us / zlm_us, 3),
             }
         if world == 1 and not args.no_cpu_baseline:
