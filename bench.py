@@ -418,6 +418,9 @@ def run_ours(args):
 
     # ---- reduce over ranks: the slowest rank's time; rows summed
     ms, ms_e2e, status_f = max_over_ranks([ms, ms_e2e, float(status)], device=device)
+    # After the timed region, on more than one rank with request batches: the
+    # vocab-sharded path on the same ranks (every rank takes part).
+    shard_check = vocab_shard_check(device, world, rank) if (world > 1 and not sharded) else None
     status = int(status_f)
     rows_total = B * world
     if sharded:
@@ -475,6 +478,8 @@ def run_ours(args):
             "device_status": status,
             "clocks": clk,
         }
+        if shard_check is not None:
+            line["vocab_shard_check"] = shard_check
         if world == 1:
             line["verify_roofline"] = measure_verify(device, V, peak)
             # The z / lm_head pass: tensor-bound once its passes are wide; its
@@ -509,6 +514,55 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def vocab_shard_check(device, world, rank, seed=7, B=4, S=15, H=512, E=1024, V=151936):
+    """The vocab-sharded draft block across all `world` ranks of this job (fc2
+    and lm_head rows split, per-step argmax exchanged over NVLink inside the
+    kernels) on one small head with the full vocabulary, every rank holding the
+    same weights and inputs: whether every rank drafts the same tokens, how many
+    equal the unsharded runner's (rank 0; the shards split the fp32 sums at
+    other points, so a near-tie may go either way), the status words, and the
+    sharded block's time (CUDA events, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from domino_b200 import DraftCorrectionGraphRunner
+    from domino_b200.parallel import max_over_ranks
+
+    draft, target = build_modules(H, H, E, V, device, seed)
+    r = DraftCorrectionGraphRunner(draft, target, B, S, H, H, V, 1, device, use_graph=False, vocab_shard=True)
+    g = torch.Generator(device=device).manual_seed(seed + 1)
+    ph = torch.randn(B, S, H, generator=g, device=device).to(torch.bfloat16)
+    last = torch.randint(0, V, (B,), generator=g, device=device)
+    for _ in range(2):
+        verify, _ = r.draft_block(last, ph)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    a.record()
+    for _ in range(5):
+        verify, _ = r.draft_block(last, ph)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / 5
+    status = r.status()
+    gathered = [torch.empty_like(verify) for _ in range(world)]
+    dist.all_gather(gathered, verify)
+    same = all(torch.equal(gathered[0], t) for t in gathered)
+    us, status_f = max_over_ranks([us, float(status)], device=device)
+    r.close()
+    out = None
+    if rank == 0:
+        ref = DraftCorrectionGraphRunner(draft, target, B, S, H, H, V, 1, device, use_graph=False)
+        v1, _ = ref.draft_block(last, ph)
+        out = {"ranks": world, "head": f"H=G={H} E={E} V={V}, batch {B}, block {S + 1}",
+               "tokens_equal_across_ranks": bool(same),
+               "fraction_equal_to_unsharded": round(float((v1 == verify).float().mean()), 4),
+               "status_max": int(status_f), "us_per_block_sharded": round(us, 1)}
+        ref.close()
+    dist.barrier()
+    return out
 
 
 def measure_verify(device, V, peak, B=16, K1=16, iters=20):

@@ -325,9 +325,11 @@ def test_fused_cell_matches_separate_cell_exactly(B, P, monkeypatch):
     assert rs.status() == 0 and rf.status() == 0
 
 
-@pytest.mark.parametrize("B", [6, 20, 32])
-@pytest.mark.parametrize("shape", ["DD_WIDE_PAIR=1", "DD_WIDE_EPI_WARPS=4", "DD_WIDE_TWO_PER_SM=0"])
-def test_wide_pass_launch_shapes(B, shape, monkeypatch):
+@pytest.mark.parametrize("B,shape,dtype", [
+    (B, shape, torch.bfloat16) for B in (6, 20, 32)
+    for shape in ("DD_WIDE_PAIR=1", "DD_WIDE_EPI_WARPS=4", "DD_WIDE_TWO_PER_SM=0")
+] + [(32, "DD_WIDE_PAIR=0", torch.float16), (32, "DD_WIDE_PAIR=1", torch.float16), (6, "DD_WIDE_PAIR=0", torch.float16)])
+def test_wide_pass_launch_shapes(B, shape, dtype, monkeypatch):
     """The z / lm_head pass and the table build under each launch shape of
     the wide passes: CTA pairs (M = 256 tiles, cta_group::2), one epilogue
     warpgroup instead of two, one CTA per SM at N <= 128.  The lm_head and
@@ -335,10 +337,10 @@ def test_wide_pass_launch_shapes(B, shape, monkeypatch):
     an empty half.  Base logits against the oracle's lm_head, tokens by
     teacher forcing, the table against the default launch shape."""
     H, G, E, S, P, V = 128, 128, 320, 15, 2, 4741
-    draft, target = random_modules(H, G, E, V, seed=57 + B, fc2_std=0.08)
+    draft, target = random_modules(H, G, E, V, seed=57 + B, fc2_std=0.08, dtype=dtype)
     K = P - 1 + S
     g = torch.Generator().manual_seed(B)
-    ph = torch.randn(B, K, H, generator=g).cuda().bfloat16()
+    ph = torch.randn(B, K, H, generator=g).cuda().to(dtype)
     last = torch.randint(0, V, (B,), generator=g).cuda()
     ref_runner = make_runner(draft, target, B, S, H, G, V, P, use_graph=False)
     name, val = shape.split("=")
@@ -350,7 +352,8 @@ def test_wide_pass_launch_shapes(B, shape, monkeypatch):
     verify, base = r.draft_block(last, ph)
     assert r.status() == 0
     lm = target.lm_head.weight.detach().float().cpu().numpy()
-    base_ref = O.lm_head(ph.float().cpu().numpy(), lm, "bf16")
+    dt = "fp16" if dtype == torch.float16 else "bf16"
+    base_ref = O.lm_head(ph.float().cpu().numpy(), lm, dt)
     base_np = base.float().cpu().numpy()
     assert np.all(np.abs(base_np - base_ref) <= TOL + TOL * np.abs(base_ref))
     v = verify.cpu().numpy()
@@ -358,6 +361,6 @@ def test_wide_pass_launch_shapes(B, shape, monkeypatch):
     prefix_ids = torch.from_numpy(v[:, :P]).cuda()
     out = r(prefix_ids, ph[:, P - 1:], base[:, P - 1:])
     assert torch.equal(out.cpu(), torch.from_numpy(v[:, P:]))
-    teacher_forced_check(oracle_weights(draft, target), prefix_ids, ph[:, P - 1:], base[:, P - 1:], out)
+    teacher_forced_check(oracle_weights(draft, target, dt), prefix_ids, ph[:, P - 1:], base[:, P - 1:], out)
     r.close()
     ref_runner.close()
