@@ -133,6 +133,7 @@ struct dd_handle {
   int rollout_mode = 1;
   int min_units_per_cta = 8;
   int l2_prefetch_kb = 0;  // DD_L2_PREFETCH_KB: weight bytes per CTA prefetched into L2 past the ring
+  int l2_keep_mb = 0;      // DD_L2_KEEP_MB: s / gh weight bytes loaded evict_last, to stay in L2 across steps
   int middle = MID_SILU;    // dd_set_middle: the correction MLP's activation (and numerics)
   int fuse_cell = 0;
   int base_stage = 1;      // DD_BASE_STAGE: fc2 loads base-logit tiles by TMA at batch > 4       // DD_FUSE_CELL=1: the GRU cell runs in the fc2 launch's tail (measured slower: off)
@@ -321,6 +322,20 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   p.stages = std::max(p.base_stage_bytes || wide2 ? 3 : 4,
                       std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
   p.l2_prefetch_units = pair ? 0 : (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
+  // The s / gh weights (read once per step, ~109 MB at E = 1024) can stay in
+  // the 126 MB L2 from one step to the next while fc2 streams past them
+  // evict_first: segments that fit the budget, W_hh first, load evict_last.
+  p.w_keep[0] = p.w_keep[1] = 0;
+  if constexpr (kPhase == PH_SGH || kPhase == PH_GH) {
+    long long left = (long long)h->l2_keep_mb << 20;
+    for (int s = p.nseg - 1; s >= 0; --s) {
+      const long long bytes = (long long)p.seg[s].rows * p.K * (long long)sizeof(T);
+      if (bytes <= left) {
+        p.w_keep[s] = 1;
+        left -= bytes;
+      }
+    }
+  }
   // X-row-major outputs (z, base logits, the table): a staging area per
   // epilogue warpgroup; passes wider than 128 columns (one CTA per SM) get two
   // warpgroups.
@@ -1007,7 +1022,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
 // DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE,
-// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR) over the defaults of a fresh
+// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -1029,6 +1044,7 @@ void read_launch_env(dd_handle* h) {
   h->max_nacc = env_int("DD_NACC", d.max_nacc, 1, 4);
   h->tmem_cols_per_cta = env_int("DD_TMEM_COLS", d.tmem_cols_per_cta, 32, 512);
   h->l2_prefetch_kb = env_int("DD_L2_PREFETCH_KB", d.l2_prefetch_kb, 0, 4096);
+  h->l2_keep_mb = env_int("DD_L2_KEEP_MB", d.l2_keep_mb, 0, 120);
   h->fuse_cell = env_int("DD_FUSE_CELL", d.fuse_cell, 0, 1);
   h->base_stage = env_int("DD_BASE_STAGE", d.base_stage, 0, 1);
   h->wide_two_per_sm = env_int("DD_WIDE_TWO_PER_SM", d.wide_two_per_sm, 0, 1);

@@ -89,6 +89,7 @@ struct GemvParams {
   // buffers of base_stage_bytes after the tail; 0 = plain loads in the epilogue
   uint32_t base_stage_bytes;
   int l2_prefetch_units;  // weight tiles past the ring this CTA prefetches into L2 before waiting on its predecessor
+  int w_keep[2];     // segment s's weights are loaded with L2 evict_last (kept for the next step) instead of evict_first
   uint32_t stage_bytes;
   uint32_t b_bytes;
   int acc_slots;
@@ -788,6 +789,7 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
     if (lane == 0) {
       // ------------------------------------------------ TMA producer
       const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_keep = policy_evict_last();
       const uint64_t pol_x = policy_evict_last();
       const long long n_my = u_end - u_begin;
       const int pre = (int)(n_my < p.stages ? n_my : p.stages);
@@ -813,12 +815,13 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
         const GemvSeg& sg = p.seg[s1 ? 1 : 0];
         const long long w_tile = (s1 ? tile - p.seg[0].tiles : tile) + sg.row_off / kTileM;
         const uint8_t* pk = p.packed[s1 ? 1 : 0];
+        const uint64_t pol = p.w_keep[s1 ? 1 : 0] ? pol_keep : pol_w;
         if (pk) {
           bulk_load(ring + (size_t)stage * p.stage_bytes, pk + (size_t)(w_tile * KC + kc) * kATileBytes,
-                    kATileBytes, &full[stage], pol_w);
+                    kATileBytes, &full[stage], pol);
         } else {
           tma_load_2d(ring + (size_t)stage * p.stage_bytes, s1 ? &tmA1 : &tmA0, &full[stage], kc * kChunkK,
-                      (int)(w_tile * kTileM), pol_w);
+                      (int)(w_tile * kTileM), pol);
         }
       };
       auto load_b = [&](int stage, int kc) {
