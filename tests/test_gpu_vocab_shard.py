@@ -157,6 +157,23 @@ def _shard_worker(rank, world, port, q):
         # which are gone once this process exits
         res = {"rank": rank, "outs": outs, "verify": verify.cpu().numpy(), "status": status,
                "range": (r.vocab_begin, r.vocab_end)}
+        # A wide z / lm_head pass (20 rows x 17 positions: two passes of 176,
+        # two epilogue warpgroups) whose last pass exchanges the pure-draft
+        # prefix argmax words across the ranks.
+        B2, P2 = 20, 3
+        g2 = torch.Generator(device=f"cuda:{rank}").manual_seed(13)
+        ph2 = torch.randn(B2, P2 - 1 + S, H, generator=g2, device=f"cuda:{rank}").to(torch.bfloat16)
+        last2 = torch.randint(0, V, (B2,), generator=g2, device=f"cuda:{rank}")
+        r2 = DraftCorrectionGraphRunner(draft, target, B2, S, H, G, V, P2, torch.device("cuda", rank),
+                                        vocab_shard=True)
+        verify2, _ = r2.draft_block(last2, ph2)
+        res["status2"] = r2.status()
+        res["verify2"] = verify2.cpu().numpy()
+        dist.barrier()
+        r2.close()
+        if rank == 0:
+            ref2 = DraftCorrectionGraphRunner(draft, target, B2, S, H, G, V, P2, torch.device("cuda", 0))
+            res["ref2"] = ref2.draft_block(last2, ph2)[0].cpu().numpy()
         if rank == 0:
             ref = DraftCorrectionGraphRunner(draft, target, B, S, H, G, V, P, torch.device("cuda", 0))
             res["ref"] = ref(prefix, ph, base).cpu().numpy()
@@ -200,3 +217,13 @@ def test_vocab_shard_two_gpus_matches_unsharded():
     log_parity(f"2-GPU vocab shard: {1 - differ:.3f} of the tokens equal the unsharded runner's")
     assert differ <= 0.1
     assert np.array_equal(res[0]["verify"][:, 0], prefix[:, 0])
+    # batch 20 with a pure-draft prefix: the wide z / lm_head pass, sharded
+    for d in res:
+        assert d["status2"] == 0
+    assert np.array_equal(res[0]["verify2"], res[1]["verify2"])
+    P2 = 3
+    assert np.array_equal(res[0]["verify2"][:, :P2], res[0]["ref2"][:, :P2])  # last token + prefix argmax
+    differ2 = float(np.mean(res[0]["verify2"][:, P2:] != res[0]["ref2"][:, P2:]))
+    log_parity(f"2-GPU vocab shard, batch 20 with a 2-token prefix: prefix tokens exact, "
+               f"{1 - differ2:.3f} of the drafted tokens equal the unsharded runner's")
+    assert differ2 <= 0.1
