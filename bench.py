@@ -67,6 +67,8 @@ def parse_args():
                     help="every rank runs the same rows on its slice of the vocab (strong scaling)")
     ap.add_argument("--emb-dim", type=int, default=None, help="override E (correction-MLP width)")
     ap.add_argument("--hidden", type=int, default=None, help="override H = G (small profiling cases)")
+    ap.add_argument("--vocab", type=int, default=None,
+                    help="override V (e.g. one rank's share of a vocab-sharded head, measured on one GPU)")
     ap.add_argument("--block", type=int, default=16)
     ap.add_argument("--prefix-len", type=int, default=0, help="pure_draft_prefix_len")
     ap.add_argument("--seed", type=int, default=0)
@@ -88,6 +90,8 @@ def shapes(args):
         m["E"] = args.emb_dim
     if args.hidden:
         m["H"] = m["G"] = args.hidden
+    if args.vocab:
+        m["V"] = args.vocab
     S = args.block - 1 - args.prefix_len
     return m["H"], m["G"], m["E"], m["V"], S, args.prefix_len
 

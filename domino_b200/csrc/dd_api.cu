@@ -97,6 +97,7 @@ struct dd_handle {
   int wide_two_per_sm = 1;        // DD_WIDE_TWO_PER_SM: passes of 64 < N <= 128 run two CTAs per SM
   int wide_epi_warps = 8;         // DD_WIDE_EPI_WARPS: epilogue warps of z / lm_head / table passes with N > 128
   int wide_pair = 0;              // DD_WIDE_PAIR: those passes as CTA pairs (M = 256 tiles, cta_group::2)
+  int even_cut_pct = 60;          // DD_EVEN_CUT_PCT: slot fill from which weight streams cut tiles evenly
   int tmem_cols_per_cta = 128;    // DD_TMEM_COLS
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
   // Vocab sharding (dd_set_vocab_shard): this rank owns vocab rows
@@ -372,14 +373,17 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   int grid = (int)std::min<long long>(slots, allow_split ? std::max<long long>(1, p.units / h->min_units_per_cta) : tiles);
   // Weight streams (N <= 64) with no more tiles than slots: every tile is cut
   // into the same number k <= 4 of CTA ranges (k = 1: one whole tile per CTA),
-  // as long as that uses at least half the slots.  A finisher then adds at
-  // most k - 1 partials, where a stream-K cut over all slots can leave it a
-  // longer chain than the extra slots save (s / gh at E = 12288: 192 tiles,
-  // k = 1; at E = 1024: 104 tiles, k = 2).  Wider passes are closer to
+  // as long as that fills a clear majority of the slots (even_cut_pct, 60 %).
+  // A finisher then adds at most k - 1 partials, where a stream-K cut over all
+  // slots can leave it a longer chain than the extra slots save (s / gh at
+  // E = 12288: 192 tiles, k = 1; at E = 1024: 104 tiles, k = 2).  Near half the
+  // slots the cut leaves about one CTA per SM, which streams at the one-CTA
+  // rate (~5.3 TB/s): fc2 of an 8-way vocab shard (149 tiles) took 148 µs that
+  // way against 127 µs over all slots.  Wider passes are closer to
   // tensor-bound and keep every SM.
   if (allow_split && p.N <= 64 && tiles <= slots) {
     const long long k = std::min<long long>(4, slots / tiles);
-    if (2LL * tiles * k >= slots) grid = (int)(tiles * k);
+    if (100LL * tiles * k >= (long long)h->even_cut_pct * slots) grid = (int)(tiles * k);
   }
   if (grid < 1) grid = 1;
   int rc = DD_OK;
@@ -1022,7 +1026,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
 // DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE,
-// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB) over the defaults of a fresh
+// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB, DD_EVEN_CUT_PCT) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -1050,6 +1054,7 @@ void read_launch_env(dd_handle* h) {
   h->wide_two_per_sm = env_int("DD_WIDE_TWO_PER_SM", d.wide_two_per_sm, 0, 1);
   h->wide_epi_warps = env_int("DD_WIDE_EPI_WARPS", d.wide_epi_warps, 4, 8) == 8 ? 8 : 4;
   h->wide_pair = env_int("DD_WIDE_PAIR", d.wide_pair, 0, 1);
+  h->even_cut_pct = env_int("DD_EVEN_CUT_PCT", d.even_cut_pct, 0, 101);
 }
 
 }  // namespace
