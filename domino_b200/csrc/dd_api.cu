@@ -306,7 +306,13 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   // CTA pairs: the caller encoded the X map with half-height boxes.
   const bool pair = kXRowMajor && p.b_box_rows > 0 && 2 * p.b_box_rows == p.N && wide_pair_pass(h, p.N) &&
                     !p.packed[0] && !p.packed[1];
-  if (!pair) p.b_box_rows = p.N;
+  if (!pair) {
+    // A half-height X map only makes sense for a pair launch: its loads would
+    // deliver half the bytes a lone CTA's stage waits for.
+    if (p.b_box_rows > 0 && p.b_box_rows != p.N)
+      return fail(h, DD_EINVAL, "X map with %d-row boxes for a %d-row pass without CTA pairs", p.b_box_rows, p.N);
+    p.b_box_rows = p.N;
+  }
   p.tiles128 = tiles;
   p.units = (long long)(pair ? (tiles + 1) / 2 : tiles) * p.KC;
   p.b_bytes = (uint32_t)p.b_box_rows * 128u;
@@ -318,8 +324,9 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   const uint32_t ring_budget =
       p.N > 64 ? (wide2 ? 3u * p.stage_bytes : 196u * 1024u)
                : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
-  // At least four stages, three when the base-logit buffers take the room
-  // of the fourth (batch 32), so that two CTAs still share an SM.
+  // At least four stages; three when the base-logit buffers take the room of
+  // the fourth (fc2 above batch 8, whose stages outgrow 18 KB) or for the
+  // two-per-SM wide passes, so that two CTAs still share an SM.
   p.stages = std::max(p.base_stage_bytes || wide2 ? 3 : 4,
                       std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
   p.l2_prefetch_units = pair ? 0 : (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
