@@ -321,9 +321,18 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   // up to N = 128 three stages of at most 32 KB and 2 x 128 TMEM columns
   // leave room for a second CTA on the SM.  Narrower passes: the class ring.
   const bool wide2 = p.N > 64 && p.N <= 128 && h->wide_two_per_sm;
-  const uint32_t ring_budget =
+  uint32_t ring_budget =
       p.N > 64 ? (wide2 ? 3u * p.stage_bytes : 196u * 1024u)
                : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
+  // fc2 with base-logit staging: four stages whenever two CTAs with four
+  // still fit on an SM (batch 9-16: 20 KB stages, 80 KB, past the 72 KB ring
+  // budget; at batch 16, E = 12288 fc2 584 -> 568 us).  At batch 32 they
+  // do not, and three stay.
+  if (cls == PhaseClass::Big && p.N <= 64 && p.base_stage_bytes) {
+    const uint32_t fixed4 = 1024 + kSmemTail + 2 * p.base_stage_bytes;
+    if (2u * (4u * p.stage_bytes + fixed4 + 1024u) <= 228u * 1024u && ring_budget < 4u * p.stage_bytes)
+      ring_budget = 4u * p.stage_bytes;
+  }
   // At least four stages; three when the base-logit buffers take the room of
   // the fourth (fc2 above batch 8, whose stages outgrow 18 KB) or for the
   // two-per-SM wide passes, so that two CTAs still share an SM.
