@@ -98,6 +98,7 @@ struct dd_handle {
   int wide_epi_warps = 8;         // DD_WIDE_EPI_WARPS: epilogue warps of z / lm_head / table passes with N > 128
   int wide_pair = 0;              // DD_WIDE_PAIR: those passes as CTA pairs (M = 256 tiles, cta_group::2)
   int even_cut_pct = 60;          // DD_EVEN_CUT_PCT: slot fill from which weight streams cut tiles evenly
+  int base_bufs = 0;              // DD_BASE_BUFS: fc2 base-logit buffers, 0 = by shared-memory room, 1 or 2
   int tmem_cols_per_cta = 128;    // DD_TMEM_COLS
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
   // Vocab sharding (dd_set_vocab_shard): this rank owns vocab rows
@@ -325,13 +326,17 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
       p.N > 64 ? (wide2 ? 3u * p.stage_bytes : 196u * 1024u)
                : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
   // fc2 with base-logit staging: four stages whenever two CTAs with four
-  // still fit on an SM (batch 9-16: 20 KB stages, 80 KB, past the 72 KB ring
-  // budget; at batch 16, E = 12288 fc2 584 -> 568 us).  At batch 32 they
-  // do not, and three stay.
+  // still fit on an SM (batch 9-24: 20-22 KB stages, 80-88 KB, past the 72 KB
+  // ring budget; at batch 16, E = 12288 fc2 584 -> 568 us).  Above batch 24
+  // two CTAs with four stages fit only with one base buffer, which the
+  // producer then fills between stages.
+  p.base_bufs = 2;
   if (cls == PhaseClass::Big && p.N <= 64 && p.base_stage_bytes) {
-    const uint32_t fixed4 = 1024 + kSmemTail + 2 * p.base_stage_bytes;
-    if (2u * (4u * p.stage_bytes + fixed4 + 1024u) <= 228u * 1024u && ring_budget < 4u * p.stage_bytes)
-      ring_budget = 4u * p.stage_bytes;
+    auto fits4 = [&](int nb) {
+      return 2u * (4u * p.stage_bytes + 1024u + kSmemTail + (uint32_t)nb * p.base_stage_bytes + 1024u) <= 228u * 1024u;
+    };
+    p.base_bufs = h->base_bufs ? h->base_bufs : (fits4(2) ? 2 : (fits4(1) ? 1 : 2));
+    if (fits4(p.base_bufs) && ring_budget < 4u * p.stage_bytes) ring_budget = 4u * p.stage_bytes;
   }
   // At least four stages; three when the base-logit buffers take the room of
   // the fourth (fc2 above batch 8, whose stages outgrow 18 KB) or for the
@@ -358,7 +363,7 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   // warpgroups.
   const bool epi8 = kXRowMajor && p.N > 128 && h->wide_epi_warps == 8;
   p.xpose_bytes = kXRowMajor ? (epi8 ? 2u : 1u) * kXposeBytes : 0u;
-  const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes + 2 * p.base_stage_bytes;
+  const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes + (uint32_t)p.base_bufs * p.base_stage_bytes;
   if ((size_t)p.stages * p.stage_bytes + fixed > 227 * 1024) p.stages = (227 * 1024 - fixed) / p.stage_bytes;
   p.acc_slots = 2;  // the epilogue of one tile overlaps the next tile's MMAs (2 x 256 columns at most)
   // Up to four accumulators per slot within the per-CTA TMEM budget, so that
@@ -1042,7 +1047,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
 // DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE,
-// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB, DD_EVEN_CUT_PCT) over the defaults of a fresh
+// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB, DD_EVEN_CUT_PCT, DD_BASE_BUFS) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -1071,6 +1076,7 @@ void read_launch_env(dd_handle* h) {
   h->wide_epi_warps = env_int("DD_WIDE_EPI_WARPS", d.wide_epi_warps, 4, 8) == 8 ? 8 : 4;
   h->wide_pair = env_int("DD_WIDE_PAIR", d.wide_pair, 0, 1);
   h->even_cut_pct = env_int("DD_EVEN_CUT_PCT", d.even_cut_pct, 0, 101);
+  h->base_bufs = env_int("DD_BASE_BUFS", d.base_bufs, 0, 2);
 }
 
 }  // namespace

@@ -88,6 +88,7 @@ struct GemvParams {
   // base logits [B, 128] by TMA (the tensor map in tmA1) into one of two
   // buffers of base_stage_bytes after the tail; 0 = plain loads in the epilogue
   uint32_t base_stage_bytes;
+  int base_bufs;     // 1 or 2 base-logit buffers (one frees the room of a fourth ring stage at batch 32)
   int l2_prefetch_units;  // weight tiles past the ring this CTA prefetches into L2 before waiting on its predecessor
   int w_keep[2];     // segment s's weights are loaded with L2 evict_last (kept for the next step) instead of evict_first
   uint32_t stage_bytes;
@@ -882,18 +883,29 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
         load_b(i, kb);
         if (++kb == KC) kb = 0;
       }
-      // Base-logit tiles (PH_FC2 staging), in tile order, two buffers: the
-      // base of every tile up to `upto` is loaded once its buffer is free.
-      // They come after the wait: the base logits may be written by an
-      // earlier launch of the same call.
+      // Base-logit tiles (PH_FC2 staging), in tile order, in base_bufs
+      // buffers: the base of every tile up to `upto` is loaded once its buffer
+      // is free.  They come after the wait: the base logits may be written by
+      // an earlier launch of the same call.  With two buffers the producer
+      // may wait for one (the epilogue two tiles back frees it).  With one it
+      // must not: the buffer is freed by the epilogue of the tile before,
+      // whose MMAs need the weight stages the producer has yet to issue, so
+      // it only tests the buffer between stages and waits once its stages
+      // are all issued.
       long long btile = tile_begin;
       const long long tile_last = n_my > 0 ? (u_end - 1) / KC : tile_begin - 1;  // no units: no base tiles
-      auto base_upto = [&](long long upto) -> bool {
+      const int nb = p.base_bufs;
+      auto base_upto = [&](long long upto, bool block) -> bool {
         if (!p.base_stage_bytes) return true;
         for (; btile <= upto && btile <= tile_last; ++btile) {
           const long long n = btile - tile_begin;
-          const int bs = (int)(n & 1);
-          if (!mbar_wait_bounded(&bempty[bs], (uint32_t)(((n >> 1) & 1) ^ 1), abort_flag)) return false;
+          const int bs = (int)(n % nb);
+          const uint32_t par = (uint32_t)(((n / nb) & 1) ^ 1);
+          if (block) {
+            if (!mbar_wait_bounded(&bempty[bs], par, abort_flag)) return false;
+          } else if (!mbar_test_wait(&bempty[bs], par)) {
+            return true;  // still in use: try again after the next stage
+          }
           mbar_arrive_expect_tx(&bfull[bs], p.base_stage_bytes);
           tma_load_3d(bstage + (size_t)bs * p.base_stage_bytes, &tmA1, &bfull[bs],
                       (int)(p.base_voff + btile * kTileM), p.base_pos_off + p.t, 0);
@@ -901,12 +913,13 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
         }
         return true;
       };
-      bool ok = base_upto((u_begin + (pre > 0 ? pre - 1 : 0)) / KC);
+      bool ok = nb > 1 ? base_upto((u_begin + (pre > 0 ? pre - 1 : 0)) / KC, true)
+                       : base_upto(tile_begin, true);  // the one buffer starts free
       int stage = pre == p.stages ? 0 : pre;
       uint32_t parity = pre == p.stages ? 1u : 0u;
       long long it = pre;
       for (; ok && it < n_my; ++it) {
-        if (!base_upto(tile)) break;
+        if (!base_upto(tile, nb > 1)) break;
         if (!mbar_wait_bounded(&empty[stage], parity ^ 1u, abort_flag)) break;
         expect_stage(stage);
         load_a(stage, tile, kc);
@@ -921,6 +934,7 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
         }
       }
       *issued = it;
+      if (ok && it == n_my) base_upto(tile_last, true);  // one buffer: the bases not issued yet
     }
   } else if (warp == 1) {
     pdl_wait_primary();
@@ -1049,8 +1063,8 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
         if (p.base_stage_bytes) {
           // every tile's base load is waited for (in order), finished here or not
           const long long n = tile - u_begin / KC;
-          bslot = (int)(n & 1);
-          const bool landed = mbar_wait_bounded(&bfull[bslot], (uint32_t)((n >> 1) & 1), abort_flag);
+          bslot = (int)(n % p.base_bufs);
+          const bool landed = mbar_wait_bounded(&bfull[bslot], (uint32_t)((n / p.base_bufs) & 1), abort_flag);
           if (!named_bar_and(1, kEpiThreads, landed)) break;
           if (ept == 0) *bconsumed = n + 1;
           a.bsm = bstage + (size_t)bslot * p.base_stage_bytes;
@@ -1172,7 +1186,7 @@ __global__ void __launch_bounds__((kEpiWarp0 + kEpiWarps) * 32, kEpiWarps == 4 ?
         for (long long it = *consumed; it < *issued; ++it)
           wait_ns(&full[it % p.stages], (uint32_t)((it / p.stages) & 1), 100ull * 1000 * 1000);
         for (long long n = *bconsumed; n < *bissued; ++n)
-          wait_ns(&bfull[n & 1], (uint32_t)((n >> 1) & 1), 100ull * 1000 * 1000);
+          wait_ns(&bfull[n % p.base_bufs], (uint32_t)((n / p.base_bufs) & 1), 100ull * 1000 * 1000);
       }
       if (threadIdx.x == 0) atomicOr(p.status, 1u /* DD_STATUS_TIMEOUT */);
       __syncthreads();
