@@ -99,6 +99,7 @@ struct dd_handle {
   int wide_pair = 0;              // DD_WIDE_PAIR: those passes as CTA pairs (M = 256 tiles, cta_group::2)
   int even_cut_pct = 60;          // DD_EVEN_CUT_PCT: slot fill from which weight streams cut tiles evenly
   int base_bufs = 0;              // DD_BASE_BUFS: fc2 base-logit buffers, 0 = by shared-memory room, 1 or 2
+  int wide_one_slot = 0;          // DD_WIDE_ONE_SLOT: passes above N = 128 as two one-slot CTAs per SM
   int tmem_cols_per_cta = 128;    // DD_TMEM_COLS
   CUtensorMap tm_wz, tm_ws, tm_fc2, tm_whh, tm_lm, tm_mid, tm_h[2];
   // Vocab sharding (dd_set_vocab_shard): this rank owns vocab rows
@@ -322,8 +323,12 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   // up to N = 128 three stages of at most 32 KB and 2 x 128 TMEM columns
   // leave room for a second CTA on the SM.  Narrower passes: the class ring.
   const bool wide2 = p.N > 64 && p.N <= 128 && h->wide_two_per_sm;
+  // Above N = 128, optionally two CTAs per SM with one accumulator slot and
+  // two stages each (2 x 256 TMEM columns per SM): each CTA's epilogue
+  // overlaps the other's MMAs instead of its own.
+  const bool wide1 = kXRowMajor && p.N > 128 && !pair && h->wide_one_slot;
   uint32_t ring_budget =
-      p.N > 64 ? (wide2 ? 3u * p.stage_bytes : 196u * 1024u)
+      p.N > 64 ? (wide2 ? 3u * p.stage_bytes : wide1 ? 2u * p.stage_bytes : 196u * 1024u)
                : (uint32_t)(cls == PhaseClass::Big ? h->ring_kb_big : h->ring_kb_small) * 1024u;
   // fc2 with base-logit staging: four stages whenever two CTAs with four
   // still fit on an SM (batch 9-24: 20-22 KB stages, 80-88 KB, past the 72 KB
@@ -341,8 +346,9 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   // At least four stages; three when the base-logit buffers take the room of
   // the fourth (fc2 above batch 8, whose stages outgrow 18 KB) or for the
   // two-per-SM wide passes, so that two CTAs still share an SM.
-  p.stages = std::max(p.base_stage_bytes || wide2 ? 3 : 4,
-                      std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
+  p.stages = wide1 ? 2
+                   : std::max(p.base_stage_bytes || wide2 ? 3 : 4,
+                              std::min<int>(kMaxStages, (int)(ring_budget / p.stage_bytes)));
   p.l2_prefetch_units = pair ? 0 : (int)((long long)h->l2_prefetch_kb * 1024 / kATileBytes);
   // The s / gh weights (read once per step, ~109 MB at E = 1024) can stay in
   // the 126 MB L2 from one step to the next while fc2 streams past them
@@ -361,11 +367,11 @@ int launch_gemv_tc(dd_handle* h, const CUtensorMap& a0, const CUtensorMap* a1, c
   // X-row-major outputs (z, base logits, the table): a staging area per
   // epilogue warpgroup; passes wider than 128 columns (one CTA per SM) get two
   // warpgroups.
-  const bool epi8 = kXRowMajor && p.N > 128 && h->wide_epi_warps == 8;
+  const bool epi8 = kXRowMajor && p.N > 128 && h->wide_epi_warps == 8 && !wide1;
   p.xpose_bytes = kXRowMajor ? (epi8 ? 2u : 1u) * kXposeBytes : 0u;
   const uint32_t fixed = 1024 + kSmemTail + p.xpose_bytes + (uint32_t)p.base_bufs * p.base_stage_bytes;
   if ((size_t)p.stages * p.stage_bytes + fixed > 227 * 1024) p.stages = (227 * 1024 - fixed) / p.stage_bytes;
-  p.acc_slots = 2;  // the epilogue of one tile overlaps the next tile's MMAs (2 x 256 columns at most)
+  p.acc_slots = wide1 ? 1 : 2;  // the epilogue of one tile overlaps the next tile's MMAs (2 x 256 columns at most)
   // Up to four accumulators per slot within the per-CTA TMEM budget, so that
   // co-resident CTAs (2 per SM plus the next phase's) never wait for TMEM.
   p.nacc = 1;
@@ -1047,7 +1053,7 @@ int pack_matrix(dd_handle* h, const void* w, long long rows, long long K, long l
 // Launch-shape knobs from the environment (DD_RING_KB_*, DD_MIN_SMEM_KB_BIG,
 // DD_CTAS_PER_SM_*, DD_PACK_WEIGHTS, DD_ROLLOUT_PERSISTENT,
 // DD_MIN_UNITS_PER_CTA, DD_NACC, DD_TMEM_COLS, DD_L2_PREFETCH_KB, DD_FUSE_CELL, DD_BASE_STAGE,
-// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB, DD_EVEN_CUT_PCT, DD_BASE_BUFS) over the defaults of a fresh
+// DD_WIDE_TWO_PER_SM, DD_WIDE_EPI_WARPS, DD_WIDE_PAIR, DD_L2_KEEP_MB, DD_EVEN_CUT_PCT, DD_BASE_BUFS, DD_WIDE_ONE_SLOT) over the defaults of a fresh
 // handle.  dd_create and dd_rollout_noalloc both read them here, so the two
 // entry points always build the same launches.
 void read_launch_env(dd_handle* h) {
@@ -1077,6 +1083,7 @@ void read_launch_env(dd_handle* h) {
   h->wide_pair = env_int("DD_WIDE_PAIR", d.wide_pair, 0, 1);
   h->even_cut_pct = env_int("DD_EVEN_CUT_PCT", d.even_cut_pct, 0, 101);
   h->base_bufs = env_int("DD_BASE_BUFS", d.base_bufs, 0, 2);
+  h->wide_one_slot = env_int("DD_WIDE_ONE_SLOT", d.wide_one_slot, 0, 1);
 }
 
 }  // namespace

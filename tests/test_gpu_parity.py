@@ -327,12 +327,13 @@ def test_fused_cell_matches_separate_cell_exactly(B, P, monkeypatch):
 
 @pytest.mark.parametrize("B,shape,dtype", [
     (B, shape, torch.bfloat16) for B in (6, 20, 32)
-    for shape in ("DD_WIDE_PAIR=1", "DD_WIDE_EPI_WARPS=4", "DD_WIDE_TWO_PER_SM=0")
+    for shape in ("DD_WIDE_PAIR=1", "DD_WIDE_EPI_WARPS=4", "DD_WIDE_TWO_PER_SM=0", "DD_WIDE_ONE_SLOT=1")
 ] + [(32, "DD_WIDE_PAIR=0", torch.float16), (32, "DD_WIDE_PAIR=1", torch.float16), (6, "DD_WIDE_PAIR=0", torch.float16)])
 def test_wide_pass_launch_shapes(B, shape, dtype, monkeypatch):
     """The z / lm_head pass and the table build under each launch shape of
     the wide passes: CTA pairs (M = 256 tiles, cta_group::2), one epilogue
-    warpgroup instead of two, one CTA per SM at N <= 128.  The lm_head and
+    warpgroup instead of two, one CTA per SM at N <= 128, two one-slot CTAs
+    per SM above N = 128.  The lm_head and
     W_z rows make an odd number of 128-row tiles, so the last pair tile has
     an empty half.  Base logits against the oracle's lm_head, tokens by
     teacher forcing, the table against the default launch shape."""
